@@ -1,0 +1,114 @@
+/*
+ * gdn_b200.h -- C ABI of the B200 (sm_100a) chunked Gated DeltaNet forward.
+ *
+ * This is the drop-in boundary for the reference's forward entry point
+ *
+ *     gdn_chunk_fwd(q, k, v, beta, g) -> (o, h_final)
+ *         gdn_triton.py:113-140   (123123213weqw/v100-attention-lab)
+ *     gdn_chunk_fwd_v2(q, k, v, beta, g, C, BV, num_warps, num_stages, iters)
+ *         gdn_triton_v2.py:92-117
+ *
+ * with the semantics of gdn_ref.py:28-45 (step recurrence) and
+ * gdn_ref.py:48-99 (chunked UT form), extended by the initial state h0
+ * that gdn_ref accepts but the reference kernels ignore (gdn_triton.py:52).
+ *
+ * Plain C: device pointers, element strides and sizes; no framework types.
+ * Every entry point returns a gdn_status code; nothing throws.
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_B200_ABI_VERSION 1
+
+/* Element types (q/k/v inputs, o output). */
+enum gdn_dtype {
+  GDN_DTYPE_F32 = 0,
+  GDN_DTYPE_F16 = 1,
+  GDN_DTYPE_BF16 = 2
+};
+
+/* Status codes returned by every entry point and written to args->status. */
+enum gdn_status {
+  GDN_OK = 0,
+  GDN_ERR_INVALID_ARGUMENT = 1, /* bad pointer, shape, stride or dtype       */
+  GDN_ERR_UNSUPPORTED = 2,      /* valid request this build does not handle  */
+  GDN_ERR_ALIGNMENT = 3,        /* base/stride not 16-byte aligned (TMA)     */
+  GDN_ERR_CUDA = 4,             /* a CUDA runtime call failed                */
+  GDN_ERR_TIMEOUT = 5,          /* a device-side bounded wait expired        */
+  GDN_ERR_NO_DEVICE = 6         /* no sm_100 device is current               */
+};
+
+/*
+ * Arguments of one forward call.  Shapes follow the reference
+ * (gdn_triton.py:116-117, gdn_ref.py:11-14):
+ *   q, k  [B, T, H, K]   in_dtype     (last dim contiguous)
+ *   v     [B, T, H, V]   in_dtype     (last dim contiguous)
+ *   beta  [B, T, H]      float32
+ *   g     [B, T, H]      float32      (log decay, <= 0)
+ *   h0    [B, H, V, K]   float32      contiguous, or NULL for a zero state
+ *   o     [B, T, H, V]   out_dtype    (last dim contiguous)
+ *   ht    [B, H, V, K]   float32      contiguous, or NULL to skip the store
+ * Strides are in elements, for the (b, t, h) dimensions.
+ * T need not be a multiple of chunk_size: the tail chunk is zero-padded on
+ * the device with the padding rule of gdn_ref.py:102-114 (q=k=v=0, beta=0,
+ * g=0), so o[t >= T] is never written and the state is unaffected.
+ */
+typedef struct gdn_fwd_args {
+  int32_t abi_version; /* must be GDN_B200_ABI_VERSION */
+  int32_t B, T, H, K, V;
+  int32_t chunk_size; /* C: 64 */
+  int32_t in_dtype;   /* GDN_DTYPE_F16 or GDN_DTYPE_BF16 */
+  int32_t out_dtype;  /* GDN_DTYPE_F16, GDN_DTYPE_BF16 or GDN_DTYPE_F32 */
+  int32_t block_v;    /* V columns per CTA (32 or 64); 0 = choose */
+  const void* q;
+  int64_t q_stride[3];
+  const void* k;
+  int64_t k_stride[3];
+  const void* v;
+  int64_t v_stride[3];
+  const float* beta;
+  int64_t beta_stride[3];
+  const float* g;
+  int64_t g_stride[3];
+  const float* h0;
+  void* o;
+  int64_t o_stride[3];
+  float* ht;
+  int32_t* status; /* optional device int; the kernel ORs error bits into it */
+} gdn_fwd_args;
+
+/*
+ * Launch the fused chunked GDN forward on `stream` (a cudaStream_t; NULL is
+ * the legacy default stream).  Asynchronous: returns after the launch.
+ * Replaces gdn_chunk_fwd (gdn_triton.py:113) / gdn_chunk_fwd_v2
+ * (gdn_triton_v2.py:92); the caller owns and allocates o and ht, as the
+ * reference allocates them inside its wrapper (gdn_triton.py:126-127).
+ */
+int gdn_fwd_sm100(const gdn_fwd_args* args, void* stream);
+
+/*
+ * Chunk-parallel WY/UT preparation only (the per-chunk, state-independent
+ * stage of gdn_ref.py:76-85): for every chunk writes
+ *   W = (I+A)^-1 (beta exp(b) k)   [B, H, NT, C, K] float32
+ *   U = (I+A)^-1 (beta v)          [B, H, NT, C, V] float32
+ * with NT = ceil(T / C).  Used to test that stage in isolation.
+ */
+int gdn_wy_prep_sm100(const gdn_fwd_args* args, float* W, float* U, void* stream);
+
+/* Human-readable text of a gdn_status code. */
+const char* gdn_status_string(int code);
+
+/* GDN_B200_ABI_VERSION of the loaded library. */
+int gdn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */

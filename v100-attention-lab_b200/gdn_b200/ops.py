@@ -1,0 +1,209 @@
+"""Python entry points of the B200 chunked Gated DeltaNet forward.
+
+``gdn_chunk_fwd`` is the drop-in for the reference's
+``gdn_triton.gdn_chunk_fwd(q, k, v, beta, g)`` (gdn_triton.py:113-140):
+same positional order (q, k, v, beta, g), same shapes, same outputs
+(o in q's dtype, the final state in fp32 with K contiguous).  It also takes
+the initial state and chunk size that ``gdn_ref.gdn_chunk_ref`` accepts
+(gdn_ref.py:48) and that the reference kernels ignore (gdn_triton.py:52).
+
+Everything runs in the sm_100a library through its C ABI; if the library is
+missing, or the device is not a B200, the call raises instead of falling back.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+__all__ = ["gdn_chunk_fwd", "gdn_chunk_fwd_v2", "gdn_wy_prep", "GdnError", "check_status"]
+
+
+class GdnError(RuntimeError):
+    """Error reported by the native library."""
+
+    def __init__(self, code: int, where: str):
+        self.code = int(code)
+        super().__init__(f"{where}: {_lib.status_string(code)} (status {code})")
+
+
+_DTYPES = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
+_status_words: dict[int, torch.Tensor] = {}
+
+
+def _status_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _status_words.get(idx)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_words[idx] = w
+    return w
+
+
+def check_status(device=None) -> None:
+    """Synchronise ``device`` and raise if any kernel launched there aborted.
+
+    Kernels never hang: a device-side wait that expires aborts the CTA and
+    records GDN_ERR_TIMEOUT in a per-device status word, read here.
+    """
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    w = _status_word(dev)
+    val = int(w.item())
+    if val:
+        w.zero_()
+        code = max(c for c in range(1, 8) if val & (1 << c))
+        raise GdnError(code, "gdn_b200 kernel")
+
+
+def _check_inputs(q, k, v, beta, g):
+    tensors = {"q": q, "k": k, "v": v, "beta": beta, "g": g}
+    for name, t in tensors.items():
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor (got device {t.device})")
+    dev = q.device
+    for name, t in tensors.items():
+        if t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, q is on {dev}")
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("q, k, v must be [B, T, H, K] / [B, T, H, V]")
+    B, T, H, K = q.shape
+    if tuple(k.shape) != (B, T, H, K):
+        raise ValueError(f"k shape {tuple(k.shape)} != q shape {tuple(q.shape)}")
+    if tuple(v.shape[:3]) != (B, T, H):
+        raise ValueError(f"v shape {tuple(v.shape)} does not match q's [B, T, H]")
+    if tuple(beta.shape) != (B, T, H) or tuple(g.shape) != (B, T, H):
+        raise ValueError(f"beta and g must be [B, T, H] = {(B, T, H)}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError(f"q, k, v must share a dtype (got {q.dtype}, {k.dtype}, {v.dtype})")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise NotImplementedError(f"gdn_b200 takes fp16 or bf16 q/k/v (got {q.dtype})")
+    for name in ("q", "k", "v"):
+        if tensors[name].stride(-1) != 1:
+            raise ValueError(f"{name} must have a contiguous last dimension")
+    return B, T, H, K, v.shape[-1]
+
+
+def _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status) -> _lib.GdnFwdArgs:
+    B, T, H, K = q.shape
+    a = _lib.GdnFwdArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.B, a.T, a.H, a.K, a.V = B, T, H, K, v.shape[-1]
+    a.chunk_size = int(chunk_size)
+    a.in_dtype = _DTYPES[q.dtype]
+    a.out_dtype = _DTYPES[o.dtype] if o is not None else _lib.DTYPE_F32
+    a.block_v = int(block_v)
+    for name, t in (("q", q), ("k", k), ("v", v), ("beta", beta), ("g", g)):
+        setattr(a, name, t.data_ptr())
+        st = getattr(a, name + "_stride")
+        st[0], st[1], st[2] = t.stride(0), t.stride(1), t.stride(2)
+    a.h0 = h0.data_ptr() if h0 is not None else None
+    if o is not None:
+        a.o = o.data_ptr()
+        a.o_stride[0], a.o_stride[1], a.o_stride[2] = o.stride(0), o.stride(1), o.stride(2)
+    a.ht = ht.data_ptr() if ht is not None else None
+    a.status = status.data_ptr() if status is not None else None
+    return a
+
+
+def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output_dtype=None,
+                  output_final_state=True, block_v=0, check=False):
+    """Chunked Gated DeltaNet forward on a B200.
+
+    Args:
+        q, k: [B, T, H, K] fp16/bf16 (last dim contiguous)
+        v:    [B, T, H, V] same dtype
+        beta: [B, T, H] (cast to fp32 if needed)
+        g:    [B, T, H] log decay (<= 0), cast to fp32 if needed
+        initial_state: optional [B, H, V, K] state h0 (fp32 is used)
+        chunk_size: C (this build: 64)
+        output_dtype: dtype of o (default q.dtype, as gdn_triton.py:126)
+        output_final_state: return the final state (else None)
+        block_v: V columns per CTA (0 = choose)
+        check: synchronise and raise if the kernel reported an error
+    Returns:
+        (o [B, T, H, V], h_final [B, H, V, K] fp32 or None)
+
+    T need not be a multiple of chunk_size: the tail is padded on the device
+    with the rule of gdn_ref.py:102-114, without the host-side copies of
+    gdn_triton.py:122-125.
+    """
+    B, T, H, K, V = _check_inputs(q, k, v, beta, g)
+    lib = _lib.load()
+    dev = q.device
+    beta = beta if beta.dtype == torch.float32 else beta.float()
+    g = g if g.dtype == torch.float32 else g.float()
+    h0 = None
+    if initial_state is not None:
+        if tuple(initial_state.shape) != (B, H, V, K):
+            raise ValueError(f"initial_state must be [B, H, V, K] = {(B, H, V, K)}")
+        if initial_state.device != dev:
+            raise ValueError("initial_state must be on q's device")
+        h0 = initial_state.to(torch.float32).contiguous()
+    out_dtype = q.dtype if output_dtype is None else output_dtype
+    if out_dtype not in _DTYPES:
+        raise ValueError(f"unsupported output_dtype {out_dtype}")
+    o = torch.empty(B, T, H, V, dtype=out_dtype, device=dev)
+    ht = torch.empty(B, H, V, K, dtype=torch.float32, device=dev) if output_final_state else None
+    status = _status_word(dev)
+    args = _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.gdn_fwd_sm100(ctypes.byref(args), ctypes.c_void_p(stream))
+    if rc != _lib.OK:
+        _raise(rc, "gdn_fwd_sm100")
+    if check:
+        with torch.cuda.device(dev):
+            check_status(dev)
+    return o, ht
+
+
+def gdn_chunk_fwd_v2(q, k, v, beta, g, C=64, BV=32, num_warps=4, num_stages=1, iters=3, **kw):
+    """Keyword-compatible stand-in for ``gdn_chunk_fwd_v2`` (gdn_triton_v2.py:92).
+
+    C and BV map to ``chunk_size`` and ``block_v``.  num_warps, num_stages and
+    iters tune the reference's Triton kernel and its Newton-Schulz solve; this
+    implementation inverts (I + A) exactly, so they have no effect.
+    """
+    del num_warps, num_stages, iters
+    return gdn_chunk_fwd(q, k, v, beta, g, chunk_size=C, block_v=BV, **kw)
+
+
+def gdn_wy_prep(q, k, v, beta, g, chunk_size=64, check=True):
+    """The chunk-parallel WY/UT stage alone (gdn_ref.py:76-85).
+
+    Returns (W [B, H, NT, C, K], U [B, H, NT, C, V]) in fp32 for every chunk,
+    computed by the same device code as the fused forward.
+    """
+    B, T, H, K, V = _check_inputs(q, k, v, beta, g)
+    lib = _lib.load()
+    dev = q.device
+    beta = beta if beta.dtype == torch.float32 else beta.float()
+    g = g if g.dtype == torch.float32 else g.float()
+    NT = -(-T // chunk_size)
+    W = torch.empty(B, H, NT, chunk_size, K, dtype=torch.float32, device=dev)
+    U = torch.empty(B, H, NT, chunk_size, V, dtype=torch.float32, device=dev)
+    status = _status_word(dev)
+    args = _fill_args(q, k, v, beta, g, None, None, None, chunk_size, 0, status)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.gdn_wy_prep_sm100(ctypes.byref(args), ctypes.c_void_p(W.data_ptr()),
+                                   ctypes.c_void_p(U.data_ptr()), ctypes.c_void_p(stream))
+    if rc != _lib.OK:
+        _raise(rc, "gdn_wy_prep_sm100")
+    if check:
+        with torch.cuda.device(dev):
+            check_status(dev)
+    return W, U
+
+
+def _raise(rc: int, where: str):
+    if rc in (_lib.ERR_INVALID_ARGUMENT, _lib.ERR_ALIGNMENT):
+        raise ValueError(f"{where}: {_lib.status_string(rc)}")
+    if rc == _lib.ERR_UNSUPPORTED:
+        raise NotImplementedError(f"{where}: {_lib.status_string(rc)}")
+    raise GdnError(rc, where)
