@@ -1,0 +1,397 @@
+"""Benchmark of the chunked Gated DeltaNet forward (replaces the reference's bench_gdn.py).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3|4]
+
+One JSON line on stdout (rank 0).  Metric: GDN fwd Mtokens/s (tokens = B*T)
+on BASELINE config 2 (B=2, T=4096, H=16, K=V=128, bf16, C=64, h0 ~ N(0, 0.1)).
+
+* ``value``     device-resident throughput: inputs already in HBM, K launches
+                replayed from a CUDA graph, CUDA events around the K steps on
+                the launching stream, max over ranks.
+* ``e2e``       the same metric through the public Python API with pinned host
+                buffers: every step copies its inputs host->device and reads o
+                and the final state back.
+* ``roofline``  the kernel's algorithmic bytes per launch / its average
+                duration, against the measured HBM copy bandwidth.
+* ``cpu_baseline`` the CPU oracle (numpy port of gdn_ref's chunked path) on the
+                host cores, rank 0 at N=1 only.
+
+With N > 1 (torchrun), each rank owns a disjoint block of (batch, head)
+pairs of a global batch of 2*N sequences (weak scaling); the hot path has no
+collective.  ``--impl reference`` times the reference's CPU algorithm
+(the oracle port; the reference is pure Python and has no GPU path of its own
+to install here) on the same config and prints the same line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "v100-attention-lab_b200"), ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "GDN fwd Mtokens/s (B2 H16 K=V=128 T4096 bf16) + % of roofline"
+UNIT = "Mtokens/s"
+
+CONFIGS = {
+    1: dict(name="config1: B2 T2048 H8 K=V=128 fp16 C64 h0=0", B=2, T=2048, H=8, dtype="fp16", h0=False, gate_mean=0.0),
+    2: dict(name="config2: B2 T4096 H16 K=V=128 bf16 C64 h0~N(0,0.1)", B=2, T=4096, H=16, dtype="bf16", h0=True,
+            gate_mean=0.0),
+    3: dict(name="config3: B2 T65536 H16 K=V=128 bf16 C64 g=logsigmoid(N(2,1))", B=2, T=65536, H=16, dtype="bf16",
+            h0=False, gate_mean=2.0),
+    4: dict(name="config4: B8 T8192 H32 K=V=128 bf16 C64 h0~N(0,0.1), (b,h) sharded", B=8, T=8192, H=32, dtype="bf16",
+            h0=True, gate_mean=0.0),
+}
+K_DIM = V_DIM = 128
+CHUNK = 64
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def algo_bytes(B, T, H, s_in=2, s_out=2, h0=True):
+    """Algorithmic HBM bytes of one forward: q,k,v read, o written, beta/g read,
+    h0 read (if given) and the final state written."""
+    per_tok_head = (2 * K_DIM + V_DIM) * s_in + V_DIM * s_out + 8
+    state = K_DIM * V_DIM * 4 * (2 if h0 else 1)
+    return B * T * H * per_tok_head + B * H * state
+
+
+def algo_flops(B, T, H, C=CHUNK):
+    """6KV + 4CK + 2CV + C(K+V) flops per token per head."""
+    K, V = K_DIM, V_DIM
+    return B * T * H * (6 * K * V + 4 * C * K + 2 * C * V + C * (K + V))
+
+
+# ----------------------------------------------------------------------------- inputs
+def make_inputs(cfg, B, seed, device, gen_device=None):
+    """Seeded synthetic inputs with the BASELINE distributions, generated on the GPU."""
+    dt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
+    T, H = cfg["T"], cfg["H"]
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def l2n(x):
+        return (x / torch.sqrt((x * x).sum(-1, keepdim=True) + 1e-6))
+
+    q = l2n(torch.randn(B, T, H, K_DIM, device=device, generator=g)).to(dt)
+    k = l2n(torch.randn(B, T, H, K_DIM, device=device, generator=g)).to(dt)
+    v = torch.randn(B, T, H, V_DIM, device=device, generator=g).to(dt)
+    beta = torch.sigmoid(torch.randn(B, T, H, device=device, generator=g))
+    gg = torch.nn.functional.logsigmoid(torch.randn(B, T, H, device=device, generator=g) + cfg["gate_mean"])
+    h0 = torch.randn(B, H, V_DIM, K_DIM, device=device, generator=g) * 0.1 if cfg["h0"] else None
+    return q, k, v, beta, gg, h0
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        try:
+            self.gpu = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            self.gpu = str(device.index or 0)
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), pw=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], swp=parts[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [r for r in rows if r["pw"] > 200.0] or rows
+        reasons = set()
+        for r in loaded:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                              ("swt", "sw_thermal_slowdown"), ("swp", "sw_power_cap")):
+                if r[key].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": rows[0]["smax"],
+                "reasons": sorted(reasons), "samples": len(loaded)}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_baseline(cfg, budget_s=12.0):
+    """Time the numpy oracle (chunked UT path, fp32) on the host cores.
+
+    Sample: the config's shape restricted to a subset of (b, h) pairs, repeated
+    until ~budget_s of CPU work; throughput is scaled to the full B*H.
+    """
+    from oracle import gdn_oracle as ora
+    T, H, B = cfg["T"], cfg["H"], cfg["B"]
+    nbh = 2
+    q, k, v, beta, g, h0 = ora.make_inputs(1, T, nbh, K_DIM, V_DIM, seed=3, gate_mean=cfg["gate_mean"],
+                                           h0_std=0.1 if cfg["h0"] else None)
+    reps, t_tot = 0, 0.0
+    while t_tot < budget_s and reps < 50:
+        t0 = time.perf_counter()
+        ora.chunked(q, k, v, beta, g, C=CHUNK, initial_state=h0, dtype=np.float32)
+        t_tot += time.perf_counter() - t0
+        reps += 1
+    t_per_pair = t_tot / reps / nbh
+    tokens_per_s = (B * T) / (t_per_pair * B * H)
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": tokens_per_s / 1e6, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"numpy fp32 chunked oracle, T={T}, {nbh} (b,h) pairs x {reps} runs "
+                      f"({t_tot:.1f} s), scaled to B*H={B * H} pairs"}
+
+
+# ----------------------------------------------------------------------------- distributed
+def dist_setup(n):
+    if n <= 1 or "RANK" not in os.environ:
+        return 0, 1, 0
+    import datetime
+    import torch.distributed as dist
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    return dist.get_rank(), dist.get_world_size(), local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------------- arms
+def run_reference(args, cfg, rank, world):
+    if rank != 0:
+        return None
+    res = []
+    for _ in range(args.warmup):
+        pass
+    samples = []
+    for _ in range(max(1, args.steps)):
+        cb = cpu_baseline(cfg, budget_s=max(2.0, 60.0 / max(1, args.steps)))
+        samples.append(cb["value"])
+        res.append(cb)
+    val = statistics.median(samples)
+    cb = dict(res[-1])
+    cb["value"] = val
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
+        "config": {"workload": cfg["name"], "B": cfg["B"], "T": cfg["T"], "H": cfg["H"], "K": K_DIM, "V": V_DIM,
+                   "chunk": CHUNK, "parallelism": "host cores"},
+        "cpu_baseline": cb,
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+def run_ours(args, cfg, rank, world, local):
+    import gdn_b200
+    from gdn_b200 import _lib
+    _lib.load()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B_rank = cfg["B"] if world == 1 else cfg["B"]  # per-rank batch (weak scaling: global B = B * world)
+    T, H = cfg["T"], cfg["H"]
+    in_bytes_one = B_rank * T * H * (2 * K_DIM + V_DIM) * 2
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size if hasattr(
+        torch.cuda.get_device_properties(dev), "L2_cache_size") else 126 * 2 ** 20
+    nsets = max(1, min(4, -(-2 * l2 // in_bytes_one)))  # rotate enough sets to exceed 2x L2
+    sets = [make_inputs(cfg, B_rank, seed=1000 * rank + s, device=dev) for s in range(nsets)]
+    out_dtype = sets[0][0].dtype
+
+    def step(s):
+        q, k, v, beta, g, h0 = sets[s % nsets]
+        return gdn_b200.gdn_chunk_fwd(q, k, v, beta, g, initial_state=h0, chunk_size=CHUNK)
+
+    # correctness guard on rank 0: one launch checked for kernel errors
+    step(0)
+    gdn_b200.check_status(dev)
+
+    # CUDA graph holding one launch per input set; replayed K / nsets times
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for s in range(nsets):
+            step(s)
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for s in range(nsets):
+            step(s)
+    reps = max(1, -(-args.steps // nsets))
+    steps = reps * nsets
+    for _ in range(max(3, -(-args.warmup // nsets))):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+
+    clocks = ClockSampler(dev)
+    if rank == 0:
+        clocks.start()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    launch_stream = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(launch_stream)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(launch_stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    if rank == 0:
+        clocks.stop()
+    ms_local = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms_local, world)
+    gdn_b200.check_status(dev)
+    tokens_all = B_rank * T * world * steps
+    value = tokens_all / (ms / 1e3) / 1e6
+    ms_per_step = ms / steps
+
+    # e2e: public API with pinned host buffers, H2D of inputs and D2H of o + h_final every step
+    host = []
+    for s in range(min(nsets, 2)):
+        host.append([None if x is None else x.cpu().pin_memory() for x in sets[s]])
+    e2e_steps = max(3, min(args.steps, 20))
+    h2d = sum(x.numel() * x.element_size() for x in host[0] if x is not None)
+    o_host = torch.empty(B_rank, T, H, V_DIM, dtype=out_dtype).pin_memory()
+    ht_host = torch.empty(B_rank, H, V_DIM, K_DIM, dtype=torch.float32).pin_memory()
+    d2h = o_host.numel() * o_host.element_size() + ht_host.numel() * 4
+
+    def e2e_step(j):
+        hq = host[j % len(host)]
+        dq = [None if x is None else x.to(dev, non_blocking=True) for x in hq]
+        o, ht = gdn_b200.gdn_chunk_fwd(*dq[:5], initial_state=dq[5], chunk_size=CHUNK)
+        o_host.copy_(o, non_blocking=True)
+        ht_host.copy_(ht, non_blocking=True)
+
+    for j in range(2):
+        e2e_step(j)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(launch_stream)
+    for j in range(e2e_steps):
+        e2e_step(j)
+    f1.record(launch_stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
+    e2e_value = B_rank * T * world * e2e_steps / (e2e_ms / 1e3) / 1e6
+
+    if rank != 0:
+        return None
+    hbm, tf, peak_src = load_peaks()
+    abytes = algo_bytes(B_rank, T, H, h0=cfg["h0"])
+    kern_s = ms_per_step / 1e3
+    achieved = abytes / kern_s / 1e9
+    flops = algo_flops(B_rank, T, H)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": "synthetic (seeded, BASELINE distributions)",
+        "config": {"workload": cfg["name"], "B_per_gpu": B_rank, "T": T, "H": H, "K": K_DIM, "V": V_DIM,
+                   "chunk": CHUNK, "global_B": B_rank * world,
+                   "l2": f"inputs rotate over {nsets} resident sets ({nsets * in_bytes_one / 1e6:.0f} MB > 2x L2)",
+                   "parallelism": f"{world} GPU(s), disjoint (batch, head) shards, no collective"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": None, "peak_source": peak_src, "algorithmic_bytes_per_launch": abytes,
+                     "tensor_frac": flops / kern_s / 1e12 / tf},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": steps,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg)
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=30)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", 0))
+        line = run_reference(args, cfg, rank, args.gpus)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        line = run_ours(args, cfg, rank, world, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -46,7 +46,9 @@ constexpr int kC = 64;    // chunk length
 constexpr int kK = 128;   // key dim
 constexpr int kV = 128;   // value dim
 constexpr int kThreads = 384;
-constexpr int kAStride = 68;  // fp32 row stride of the A/T work matrix
+constexpr int kAStride = 68;  // fp32 row stride of the A/T work matrix (column 64 holds F_m)
+constexpr int kVecN = 4;      // per-chunk vectors: b*log2(e) (cumsum), beta, e^b, e^(b_C - b)
+enum : int { V_B2 = 0, V_BETA = 1, V_EB = 2, V_DD = 3 };
 
 // ------------------------------------------------------------------ layout
 template <int BV>
@@ -66,8 +68,8 @@ struct Layout {
   static constexpr uint32_t ht16 = vt1 + ((vt_bytes + 1023) / 1024) * 1024;  // h^T fp16: 128 rows x BV*2 B
   static constexpr uint32_t u16 = ht16 + ((kK * BV * 2 + 1023) / 1024) * 1024;  // u fp16: 64 rows x BV*2 B
   static constexpr uint32_t amat = u16 + ((kC * BV * 2 + 1023) / 1024) * 1024;  // fp32 A / T
-  static constexpr uint32_t vec = amat + kC * kAStride * 4;                      // 4 x {b2[64], beta[64]}
-  static constexpr uint32_t bars = vec + 4 * 2 * kC * 4;
+  static constexpr uint32_t vec = amat + kC * kAStride * 4;  // 4 chunks x {b2, beta, e^b, e^(b_C-b)} x 64
+  static constexpr uint32_t bars = vec + 4 * kVecN * kC * 4;
   static constexpr uint32_t nbars = 40;
   static constexpr uint32_t misc = bars + nbars * 8;
   static constexpr uint32_t total = misc + 64;
@@ -126,11 +128,26 @@ struct FwdParams {
   float* w_out;  // prep-only mode
   float* u_out;
   int* status;
+  long long* trace;  // per-chunk role timestamps of CTA 0 (GDN_TRACE builds only)
   long long sb_b, sb_t, sb_h;
   long long sg_b, sg_t, sg_h;
   long long so_b, so_t, so_h;
   int B, T, H, NT, nslice;
 };
+
+// Tracing: with -DGDN_TRACE the kernel records clock64() at fixed points of
+// each role for every chunk of CTA 0 into P.trace[chunk * kTraceSlots + slot].
+constexpr int kTraceSlots = 24;
+#ifdef GDN_TRACE
+#define GDN_TR(slot, chunk)                                                                  \
+  do {                                                                                       \
+    if (P.trace != nullptr && blockIdx.x == 0) P.trace[(chunk) * kTraceSlots + (slot)] = clock64(); \
+  } while (0)
+#else
+#define GDN_TR(slot, chunk) \
+  do {                      \
+  } while (0)
+#endif
 
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -192,93 +209,102 @@ __device__ __forceinline__ void st_row16(uint8_t* tile, uint32_t r, uint32_t c16
 
 // ------------------------------------------------------------------ the inverse
 // T = (I + A)^-1 for the 64x64 strictly-lower A held in `am` (row stride
-// kAStride), computed in place by the 128 prep threads:
-//   level 0: the four 16x16 diagonal blocks by column forward substitution;
-//   block rows r = 1..3: Z = A[r, :r] T[:r, :r], then T[r, :r] = -T_rr Z.
-// Same result as the forward substitution of gdn_triton.py:75-84 applied to
-// the identity; O(C^3/6) fp32 FMAs.
+// kAStride), in place, by the 128 prep threads (named barrier 1).  Eight 8x8
+// diagonal blocks are inverted by column forward substitution; three
+// doubling levels (8 -> 16 -> 32 -> 64) then apply
+//     inv([[L0, 0], [X, L1]]) = [[inv(L0), 0], [-inv(L1) X inv(L0), inv(L1)]].
+// The upper triangle of every block stays zero, so the block products can run
+// over full index ranges.  Same result as the row-by-row forward substitution
+// of gdn_triton.py:75-84 applied to the identity.
+template <int N>
+__device__ __forceinline__ void inv_level(float* am, int tid) {
+  constexpr int NTH = 128;
+  constexpr int NOUT = (64 / (2 * N)) * N * N;  // outputs per phase
+  constexpr int PER = NOUT / NTH;               // outputs per thread
+  float acc[PER];
+  // phase 1: Y = X inv(L0), X = rows N..2N-1 x cols 0..N-1 of each 2N block
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const int idx = tid + e * NTH;
+    const int pr = idx / (N * N), rem = idx % (N * N);
+    const int i = rem / N, j = rem % N, o = pr * 2 * N;
+    const float* xr = am + (o + N + i) * kAStride + o;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int m = 0; m < N; m += 4) {
+      const float4 xv = *reinterpret_cast<const float4*>(xr + m);
+      s0 = fmaf(xv.x, am[(o + m + 0) * kAStride + o + j], s0);
+      s1 = fmaf(xv.y, am[(o + m + 1) * kAStride + o + j], s1);
+      s2 = fmaf(xv.z, am[(o + m + 2) * kAStride + o + j], s2);
+      s3 = fmaf(xv.w, am[(o + m + 3) * kAStride + o + j], s3);
+    }
+    acc[e] = (s0 + s1) + (s2 + s3);
+  }
+  named_bar(1, NTH);
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const int idx = tid + e * NTH;
+    const int pr = idx / (N * N), rem = idx % (N * N);
+    am[(pr * 2 * N + N + rem / N) * kAStride + pr * 2 * N + rem % N] = acc[e];
+  }
+  named_bar(1, NTH);
+  // phase 2: T = -inv(L1) Y
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const int idx = tid + e * NTH;
+    const int pr = idx / (N * N), rem = idx % (N * N);
+    const int i = rem / N, j = rem % N, o = pr * 2 * N;
+    const float* tr = am + (o + N + i) * kAStride + o + N;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int p = 0; p < N; p += 4) {
+      const float4 tv = *reinterpret_cast<const float4*>(tr + p);
+      s0 = fmaf(tv.x, am[(o + N + p + 0) * kAStride + o + j], s0);
+      s1 = fmaf(tv.y, am[(o + N + p + 1) * kAStride + o + j], s1);
+      s2 = fmaf(tv.z, am[(o + N + p + 2) * kAStride + o + j], s2);
+      s3 = fmaf(tv.w, am[(o + N + p + 3) * kAStride + o + j], s3);
+    }
+    acc[e] = -((s0 + s1) + (s2 + s3));
+  }
+  named_bar(1, NTH);
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const int idx = tid + e * NTH;
+    const int pr = idx / (N * N), rem = idx % (N * N);
+    am[(pr * 2 * N + N + rem / N) * kAStride + pr * 2 * N + rem % N] = acc[e];
+  }
+  named_bar(1, NTH);
+}
+
 __device__ __forceinline__ void invert_unit_lower64(float* am, int ptid) {
-  const int wl = ptid >> 5, lane = ptid & 31;
-  {
-    const int r = wl, c = lane & 15;
-    float x[16];
+  if (ptid < 64) {
+    const int blk_id = ptid >> 3, c = ptid & 7;
+    float* blk = am + (8 * blk_id) * kAStride + 8 * blk_id;
+    float x[8];
 #pragma unroll
-    for (int m = 0; m < 16; ++m) x[m] = (m == c) ? 1.f : 0.f;
-    const float* blk = am + (16 * r) * kAStride + 16 * r;
+    for (int m = 0; m < 8; ++m) x[m] = (m == c) ? 1.f : 0.f;
 #pragma unroll
-    for (int t = 1; t < 16; ++t) {
-      float acc = 0.f;
+    for (int t = 1; t < 8; ++t) {
+      float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-      for (int m = 0; m < t; ++m) acc = fmaf(blk[t * kAStride + m], x[m], acc);
-      if (t > c) x[t] = -acc;
+      for (int m = 0; m < t; ++m) {
+        if (m & 1)
+          a1 = fmaf(blk[t * kAStride + m], x[m], a1);
+        else
+          a0 = fmaf(blk[t * kAStride + m], x[m], a0);
+      }
+      if (t > c) x[t] = -(a0 + a1);
     }
     __syncwarp();
-    if (lane < 16) {
-      float* dst = am + (16 * r) * kAStride + 16 * r + c;
 #pragma unroll
-      for (int t = 0; t < 16; ++t) dst[t * kAStride] = x[t];
-    }
+    for (int t = 0; t < 8; ++t) blk[t * kAStride + c] = x[t];
   }
   named_bar(1, 128);
-  const int jj = ptid & 15, rp = ptid >> 4;  // column within a block, row pair
-#pragma unroll
-  for (int r = 1; r < 4; ++r) {
-    // Z[i][16s+jj] = sum_m A[16r+i][m] T[m][16s+jj],  m in [16s, 16r)
-    float z[2][3];
-#pragma unroll
-    for (int s = 0; s < 3; ++s) z[0][s] = z[1][s] = 0.f;
-    const float* arow0 = am + (16 * r + rp) * kAStride;
-    const float* arow1 = am + (16 * r + rp + 8) * kAStride;
-#pragma unroll
-    for (int m = 0; m < 16 * r; ++m) {
-      const float a0 = arow0[m], a1 = arow1[m];
-#pragma unroll
-      for (int s = 0; s < 3; ++s) {
-        if (s < r && m >= 16 * s) {
-          const float tv = am[m * kAStride + 16 * s + jj];
-          z[0][s] = fmaf(a0, tv, z[0][s]);
-          z[1][s] = fmaf(a1, tv, z[1][s]);
-        }
-      }
-    }
-    named_bar(1, 128);
-#pragma unroll
-    for (int s = 0; s < 3; ++s) {
-      if (s < r) {
-        am[(16 * r + rp) * kAStride + 16 * s + jj] = z[0][s];
-        am[(16 * r + rp + 8) * kAStride + 16 * s + jj] = z[1][s];
-      }
-    }
-    named_bar(1, 128);
-    // T[16r+i][j] = -sum_{p<=i} T_rr[i][p] Z[p][j]
-    float tv[2][3];
-#pragma unroll
-    for (int s = 0; s < 3; ++s) tv[0][s] = tv[1][s] = 0.f;
-    const float* trr0 = am + (16 * r + rp) * kAStride + 16 * r;
-    const float* trr1 = am + (16 * r + rp + 8) * kAStride + 16 * r;
-#pragma unroll
-    for (int p = 0; p < 16; ++p) {
-      const float t0 = trr0[p], t1 = trr1[p];
-#pragma unroll
-      for (int s = 0; s < 3; ++s) {
-        if (s < r) {
-          const float zv = am[(16 * r + p) * kAStride + 16 * s + jj];
-          tv[0][s] = fmaf(t0, zv, tv[0][s]);
-          tv[1][s] = fmaf(t1, zv, tv[1][s]);
-        }
-      }
-    }
-    named_bar(1, 128);
-#pragma unroll
-    for (int s = 0; s < 3; ++s) {
-      if (s < r) {
-        am[(16 * r + rp) * kAStride + 16 * s + jj] = -tv[0][s];
-        am[(16 * r + rp + 8) * kAStride + 16 * s + jj] = -tv[1][s];
-      }
-    }
-    named_bar(1, 128);
-  }
+  inv_level<8>(am, ptid);
+  inv_level<16>(am, ptid);
+  inv_level<32>(am, ptid);
 }
+
 // ------------------------------------------------------------------ kernel
 // Abort protocol: every wait is bounded (tc.cuh).  A role that gives up sets
 // the CTA abort flag and leaves its loop; the others see the flag within a
@@ -291,11 +317,14 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
   using TC = TmemCols<BV>;
   static_assert(BV == 32, "this build implements 32-column V slices");
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-B aligned base for the swizzled tiles.  Offsetting the __shared__
+  // array itself (not an integer round trip) keeps the shared address space
+  // visible to the compiler, so every access below is an LDS/STS.
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::bars);
   uint32_t* tmem_base_p = reinterpret_cast<uint32_t*>(sm + L::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::misc + 4);
-  float* vecs = reinterpret_cast<float*>(sm + L::vec);  // [4][2][64]: b*log2(e), beta
+  float* vecs = reinterpret_cast<float*>(sm + L::vec);  // [4][kVecN][64]
   float* amat = reinterpret_cast<float*>(sm + L::amat);
 
   const int tid = threadIdx.x;
@@ -345,6 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
         tma_load_4d(kq + 16384, &P.tm_k, &bars[B_FULL + s], 64, t0, hh, bb);
         tma_load_4d(kq + 24576, &P.tm_q, &bars[B_FULL + s], 64, t0, hh, bb);
         tma_load_4d(vt, &P.tm_v, &bars[B_FULL + s], v0, t0, hh, bb);
+        GDN_TR(0, i);
       }
       issued = i + 1;
       // beta and the in-chunk cumsum of g (log2 units); zero past T, which is
@@ -365,11 +395,16 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
       }
       xb += __shfl_sync(0xffffffffu, xa, 31);
       // vec[i & 3] is free: chunk i-4's readers finished before EMPTY(i-2) completed
-      float* vec = vecs + (i & 3) * 2 * kC;
-      vec[lane] = xa;
-      vec[lane + 32] = xb;
-      vec[kC + lane] = ba;
-      vec[kC + lane + 32] = bbv;
+      const float bC = __shfl_sync(0xffffffffu, xb, 31);
+      float* vec = vecs + (i & 3) * kVecN * kC;
+      vec[V_B2 * kC + lane] = xa;
+      vec[V_B2 * kC + lane + 32] = xb;
+      vec[V_BETA * kC + lane] = ba;
+      vec[V_BETA * kC + lane + 32] = bbv;
+      vec[V_EB * kC + lane] = fast_exp2(xa);
+      vec[V_EB * kC + lane + 32] = fast_exp2(xb);
+      vec[V_DD * kC + lane] = fast_exp2(bC - xa);
+      vec[V_DD * kC + lane + 32] = fast_exp2(bC - xb);
       mbar_arrive(&bars[B_VEC + (i & 3)]);
     }
     // every issued TMA load must land before the CTA exits
@@ -380,101 +415,61 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ================================================================ MMA issuer
+    // ================================================================ MMA issuer (prep GEMMs)
+    // The chain GEMMs (D1, D2, D3) are issued by the chain warps themselves so the
+    // serial path never waits for this thread's polling loop.
     if (lane == 0) {
       constexpr uint32_t kInBf16 = Cvt<InT>::kIsBf16;
       const uint32_t id_s = idesc_f16(128, 64, kInBf16, 0, 0);
       const uint32_t id_w = idesc_f16(128, 128, kInBf16, 0, 1);
       const uint32_t id_u = idesc_f16(128, BV, kInBf16, 0, 1);
-      const uint32_t id_1 = idesc_f16(128, BV, 0, 0, 1);
-      const uint32_t id_2 = idesc_f16(128, BV, 0, 1, 1);
-      const uint32_t id_3 = idesc_f16(128, BV, 0, 0, 1);
       const uint32_t sb = smem_u32(sm);
-      int nS = 0, nW = 0, n1 = 0, n2 = 0;
-      uint64_t last = globaltimer();
-      while (kPrepOnly ? (nW < NT) : (n2 < NT)) {
-        bool prog = false;
-        if (!kPrepOnly) {
-          // chain GEMMs first: they are the critical path
-          if (n2 < n1 && mbar_test(&bars[B_U16], n2 & 1) && mbar_test(&bars[B_KFULL], n2 & 1)) {
-            tc_fence_after();
-            const uint32_t pb = sb + ((n2 & 1) ? L::p1 : L::p0);
+      // In-order: S(0), then per chunk i: W/U(i), S(i+1).  All waits suspend in
+      // hardware (try_wait), so this thread takes no issue slots while idle.
+      auto issue_s = [&](int c) -> bool {
+        if (!mbar_wait(&bars[B_FULL + (c & 1)], (c >> 1) & 1, abort_flag)) return false;
+        if (c > 0 && !mbar_wait(&bars[B_SFREE], (c - 1) & 1, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t kq = sb + ((c & 1) ? L::kq1 : L::kq0);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t bd = sdesc(sb + L::u16 + kk * 2 * L::bv_sbo, 8192, L::bv_sbo, L::bv_swz);
-              mma_f16_ss(tmem + TC::d2, sdesc(sb + L::kbar + kk * 2048, 8192, 1024, kSw128), bd, id_2, kk > 0);
-              mma_f16_ss(tmem + TC::d3, sdesc(pb + kk * 32, 16, 1024, kSw128), bd, id_3, kk > 0);
-            }
-            mma_commit(&bars[B_D2]);
-            mma_commit(&bars[B_KFREE]);
-            mma_commit(&bars[B_PFREE + (n2 & 1)]);
-            ++n2;
-            prog = true;
-          }
-          if (n1 < NT && n1 == n2 && mbar_test(&bars[B_HFULL], n1 & 1) &&
-              mbar_test(&bars[B_AFULL + (n1 & 1)], (n1 >> 1) & 1)) {
-            tc_fence_after();
-            const uint32_t ab = sb + ((n1 & 1) ? L::ahat1 : L::ahat0);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint64_t ad = sdesc(ab + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSw128);
-              const uint64_t bd = sdesc(sb + L::ht16 + kk * 2 * L::bv_sbo, 8192, L::bv_sbo, L::bv_swz);
-              mma_f16_ss(tmem + TC::d1, ad, bd, id_1, kk > 0);
-            }
-            mma_commit(&bars[B_D1]);
-            mma_commit(&bars[B_AFREE + (n1 & 1)]);
-            ++n1;
-            prog = true;
-          }
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t a = kq + (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma_f16_ss(tmem + kTmS, sdesc(a, 16, 1024, kSw128), sdesc(a, 16, 1024, kSw128), id_s, kk > 0);
         }
-        if (nW < nS && mbar_test(&bars[B_TREADY], nW & 1) && (nW == 0 || mbar_test(&bars[B_WFREE], (nW - 1) & 1)) &&
-            (nW < 2 || mbar_test(&bars[B_UFREE + (nW & 1)], ((nW >> 1) - 1) & 1))) {
-          tc_fence_after();
-          const uint32_t kq = sb + ((nW & 1) ? L::kq1 : L::kq0);
-          const uint32_t vt = sb + ((nW & 1) ? L::vt1 : L::vt0);
-          const uint32_t ts = sb + L::tstk;
-          // W = [Tw; Tb_hi] K: lanes 0-63 hold W.  B = the k tile read MN-major
-          // (d blocks of 64 are 16 KB apart in the stacked [k;q] layout).
+        mma_commit(&bars[B_SFULL]);
+        GDN_TR(1, c);
+        return true;
+      };
+      bool okm = issue_s(0);
+      for (int i = 0; i < NT && okm; ++i) {
+        okm = mbar_wait(&bars[B_TREADY], i & 1, abort_flag) &&
+              (i == 0 || mbar_wait(&bars[B_WFREE], (i - 1) & 1, abort_flag)) &&
+              (i < 2 || mbar_wait(&bars[B_UFREE + (i & 1)], ((i >> 1) - 1) & 1, abort_flag));
+        if (!okm) break;
+        tc_fence_after();
+        const uint32_t kq = sb + ((i & 1) ? L::kq1 : L::kq0);
+        const uint32_t vt = sb + ((i & 1) ? L::vt1 : L::vt0);
+        const uint32_t ts = sb + L::tstk;
+        // W = [Tw; Tb_hi] K: lanes 0-63 hold W.  B = the k tile read MN-major
+        // (d blocks of 64 are 16 KB apart in the stacked [k;q] layout).
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f16_ss(tmem + kTmW, sdesc(ts + kk * 32, 16, 1024, kSw128), sdesc(kq + kk * 2048, 16384, 1024, kSw128),
-                       id_w, kk > 0);
-          // U = [Tw | *; Tb_hi | Tb_lo] [V; V]: lanes 64-127 hold Tb_hi V + Tb_lo V.
-          const uint32_t ucol = (nW & 1) ? TC::u1 : TC::u0;
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tmem + kTmW, sdesc(ts + kk * 32, 16, 1024, kSw128), sdesc(kq + kk * 2048, 16384, 1024, kSw128),
+                     id_w, kk > 0);
+        // U = [Tw | *; Tb_hi | Tb_lo] [V; V]: lanes 64-127 hold Tb_hi V + Tb_lo V.
+        const uint32_t ucol = (i & 1) ? TC::u1 : TC::u0;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_f16_ss(tmem + ucol, sdesc(ts + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSw128),
-                       sdesc(vt + (kk & 3) * 2 * L::bv_sbo, 8192, L::bv_sbo, L::bv_swz), id_u, kk > 0);
-          mma_commit(&bars[B_WFULL]);
-          mma_commit(&bars[B_UFULL + (nW & 1)]);
-          mma_commit(&bars[B_TFREE]);
-          mma_commit(&bars[B_EMPTY + (nW & 1)]);
-          ++nW;
-          prog = true;
-        }
-        if (nS < NT && mbar_test(&bars[B_FULL + (nS & 1)], (nS >> 1) & 1) &&
-            (nS == 0 || mbar_test(&bars[B_SFREE], (nS - 1) & 1))) {
-          tc_fence_after();
-          const uint32_t kq = sb + ((nS & 1) ? L::kq1 : L::kq0);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t a = kq + (kk >> 2) * 16384 + (kk & 3) * 32;
-            mma_f16_ss(tmem + kTmS, sdesc(a, 16, 1024, kSw128), sdesc(a, 16, 1024, kSw128), id_s, kk > 0);
-          }
-          mma_commit(&bars[B_SFULL]);
-          ++nS;
-          prog = true;
-        }
-        if (prog) {
-          last = globaltimer();
-        } else {
-          if (*abort_flag) break;
-          if (globaltimer() - last > GDN_WAIT_TIMEOUT_NS) {
-            *abort_flag = 1;
-            break;
-          }
-        }
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ss(tmem + ucol, sdesc(ts + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSw128),
+                     sdesc(vt + (kk & 3) * 2 * L::bv_sbo, 8192, L::bv_sbo, L::bv_swz), id_u, kk > 0);
+        mma_commit(&bars[B_WFULL]);
+        mma_commit(&bars[B_UFULL + (i & 1)]);
+        mma_commit(&bars[B_TFREE]);
+        mma_commit(&bars[B_EMPTY + (i & 1)]);
+        GDN_TR(2, i);
+        if (i + 1 < NT) okm = issue_s(i + 1);
       }
+      if (!okm) *abort_flag = 1;
       // every issued MMA must complete before TMEM is released
       mma_commit(&bars[B_DONE]);
       volatile int never = 0;
@@ -482,24 +477,22 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
     }
     __syncwarp();
   } else if (warp == 2 || warp == 3) {
-    // ================================================================ convert
     const int t = tid - 64;  // chunk row 0..63
     for (int i = 0; i < NT; ++i) {
       const int s = i & 1, p = i & 1;
       if (!mbar_wait_warp(&bars[B_FULL + s], (i >> 1) & 1, abort_flag)) break;
       if (!mbar_wait_warp(&bars[B_VEC + (i & 3)], (i >> 2) & 1, abort_flag)) break;
-      const float* vec = vecs + (i & 3) * 2 * kC;
-      const float b2t = vec[t];
+      const float* vec = vecs + (i & 3) * kVecN * kC;
       const uint8_t* kq = sm + (s ? L::kq1 : L::kq0);
       if (!kPrepOnly) {
         // Qhat = exp(b_t) q_t -> rows 0-63 of Ahat[p]
         if (i >= 2 && !mbar_wait_warp(&bars[B_AFREE + p], ((i >> 1) - 1) & 1, abort_flag)) break;
-        const float eb = fast_exp2(b2t);
+        const float eb = vec[V_EB * kC + t];
         uint8_t* ah = sm + (p ? L::ahat1 : L::ahat0);
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
+#pragma unroll 1
+        for (int cc = 0; cc < 16; ++cc) {
+          const int cb = cc >> 3, c = cc & 7;
+          {
             const uint4 x = *reinterpret_cast<const uint4*>(kq + cb * 16384 + 8192 + sw128_off(t, c));
             const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
             uint32_t ys[4];
@@ -514,14 +507,15 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[B_AFULL + p]);
+        if (t == 0) GDN_TR(5, i);
         // Kbar = exp(b_C - b_t) k_t -> Kbar (2 d-blocks x 64 rows)
         if (i >= 1 && !mbar_wait_warp(&bars[B_KFREE], (i - 1) & 1, abort_flag)) break;
-        const float dd = fast_exp2(vec[kC - 1] - b2t);
+        const float dd = vec[V_DD * kC + t];
         uint8_t* kb = sm + L::kbar;
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
+#pragma unroll 1
+        for (int cc = 0; cc < 16; ++cc) {
+          const int cb = cc >> 3, c = cc & 7;
+          {
             const uint4 x = *reinterpret_cast<const uint4*>(kq + cb * 16384 + sw128_off(t, c));
             const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
             uint32_t ys[4];
@@ -536,12 +530,16 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[B_KFULL]);
+        if (t == 0) GDN_TR(6, i);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_EMPTY + s]);
     }
   } else if (warp >= 4 && warp < 8) {
     // ================================================================ prep
+    // Threads 0-63 own row t of A (TMEM lanes 0-63 = K K^T rows); threads
+    // 64-127 own row t of P (lanes 64-127 = Q K^T rows).  Decisions that gate
+    // barriers are made uniform with bar.red.or (bar_any).
     const int ptid = tid - 128;
     const int wl = warp - 4;
     bool ok = true;
@@ -550,72 +548,86 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
       // checkpoint: also orders the previous chunk's reads of amat before new writes
       if (bar_any(1, 128, !ok || *abort_flag)) break;
       ok = mbar_wait_warp(&bars[B_VEC + (i & 3)], (i >> 2) & 1, abort_flag) &&
-           mbar_wait_warp(&bars[B_SFULL], i & 1, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        const float* vec = vecs + (i & 3) * 2 * kC;
-        float srow[64];
-        tmem_ld32w(tmem_addr(tmem + kTmS, wl * 32, 0), srow);
-        tmem_ld32w(tmem_addr(tmem + kTmS, wl * 32, 32), srow + 32);
+           mbar_wait_warp(&bars[B_SFULL], i & 1, abort_flag) &&
+           (ptid < 64 || kPrepOnly || i < 2 ||
+            mbar_wait_warp(&bars[B_PFREE + p], ((i >> 1) - 1) & 1, abort_flag));
+      if (bar_any(1, 128, !ok || *abort_flag)) break;
+      tc_fence_after();
+      if (ptid == 0) GDN_TR(7, i);
+      const float* vec = vecs + (i & 3) * kVecN * kC;
+      // exp(b_t - b_m) = E_t F_m with E_t = 2^(b2_t - ref), F_m = 2^(ref - b2_m), valid
+      // while the in-chunk log2 range stays below 200 (no fp32 overflow); otherwise
+      // each factor is a direct exp2 of the difference.
+      const float b2first = vec[V_B2 * kC], b2last = vec[V_B2 * kC + kC - 1];
+      const float ref = 0.5f * (b2first + b2last);
+      const bool prod_form = (b2first - b2last) < 200.f;
+      if (ptid < 64) amat[ptid * kAStride + 64] = fast_exp2(ref - vec[V_B2 * kC + ptid]);
+      named_bar(2, 128);
+      {
+        const int t = ptid & 63;
+        const float b2t = vec[V_B2 * kC + t];
+        const float et = fast_exp2(b2t - ref);
+        const float bt = (ptid < 64) ? vec[V_BETA * kC + t] : 1.f;
+        float* arow = amat + t * kAStride;
+        uint8_t* pb = sm + (p ? L::p1 : L::p0);
+#pragma unroll 1
+        for (int cg = 0; cg < 4; ++cg) {
+          float s[16];
+          tmem_ld16w(tmem_addr(tmem + kTmS, wl * 32, cg * 16), s);
+          float x[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int m = cg * 16 + e;
+            const float dec = prod_form ? et * amat[m * kAStride + 64] : fast_exp2(b2t - vec[V_B2 * kC + m]);
+            // A[t][m] = beta_t exp(b_t - b_m) (k_t . k_m), m < t     (gdn_ref.py:76-80)
+            // P[t][m] = exp(b_t - b_m) (q_t . k_m),        m <= t    (gdn_ref.py:87-88)
+            const bool keep = (ptid < 64) ? (m < t) : (m <= t);
+            x[e] = keep ? bt * dec * s[e] : 0.f;
+          }
+          if (ptid < 64) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 4)
+              *reinterpret_cast<float4*>(arow + cg * 16 + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+          } else if (!kPrepOnly) {
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              uint4 w;
+              w.x = Cvt<__half>::pack(x[8 * h2 + 0], x[8 * h2 + 1]);
+              w.y = Cvt<__half>::pack(x[8 * h2 + 2], x[8 * h2 + 3]);
+              w.z = Cvt<__half>::pack(x[8 * h2 + 4], x[8 * h2 + 5]);
+              w.w = Cvt<__half>::pack(x[8 * h2 + 6], x[8 * h2 + 7]);
+              *reinterpret_cast<uint4*>(pb + sw128_off(t, 2 * cg + h2)) = w;
+            }
+          }
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[B_SFREE]);
-        if (ptid < 64) {
-          // A[t][m] = beta_t exp(b_t - b_m) (k_t . k_m), m < t   (gdn_ref.py:76-80)
-          const int t = ptid;
-          const float b2t = vec[t], bt = vec[kC + t];
-          float* arow = amat + t * kAStride;
-#pragma unroll
-          for (int m0 = 0; m0 < 64; m0 += 4) {
-            float4 a;
-            a.x = (m0 + 0 < t) ? bt * fast_exp2(b2t - vec[m0 + 0]) * srow[m0 + 0] : 0.f;
-            a.y = (m0 + 1 < t) ? bt * fast_exp2(b2t - vec[m0 + 1]) * srow[m0 + 1] : 0.f;
-            a.z = (m0 + 2 < t) ? bt * fast_exp2(b2t - vec[m0 + 2]) * srow[m0 + 2] : 0.f;
-            a.w = (m0 + 3 < t) ? bt * fast_exp2(b2t - vec[m0 + 3]) * srow[m0 + 3] : 0.f;
-            *reinterpret_cast<float4*>(arow + m0) = a;
-          }
-        } else if (!kPrepOnly) {
-          // P[t][m] = exp(b_t - b_m) (q_t . k_m), m <= t   (gdn_ref.py:87-88)
-          const int t = ptid - 64;
-          ok = (i < 2) || mbar_wait_warp(&bars[B_PFREE + p], ((i >> 1) - 1) & 1, abort_flag);
-          if (ok) {
-            const float b2t = vec[t];
-            uint8_t* pb = sm + (p ? L::p1 : L::p0);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              uint32_t w[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int m = 8 * c + 2 * e;
-                const float x0 = (m <= t) ? fast_exp2(b2t - vec[m]) * srow[m] : 0.f;
-                const float x1 = (m + 1 <= t) ? fast_exp2(b2t - vec[m + 1]) * srow[m + 1] : 0.f;
-                w[e] = Cvt<__half>::pack(x0, x1);
-              }
-              *reinterpret_cast<uint4*>(pb + sw128_off(t, c)) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars[B_AFULL + p]);
-          }
+        if (ptid >= 64 && !kPrepOnly) {
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[B_AFULL + p]);
         }
       }
-      if (bar_any(1, 128, !ok || *abort_flag)) break;
+      if (ptid == 0) GDN_TR(17, i);
+      named_bar(1, 128);
+      if (ptid == 0) GDN_TR(8, i);
       invert_unit_lower64(amat, ptid);  // T = (I + A)^-1 in place
-      const float* vec = vecs + (i & 3) * 2 * kC;
+      if (ptid == 0) GDN_TR(9, i);
       // Tstack: Tw = T diag(beta e^b) (input dtype), Tb = T diag(beta) as hi + lo
       ok = (i == 0) || mbar_wait_warp(&bars[B_TFREE], (i - 1) & 1, abort_flag);
       if (ok) {
         const int t = ptid >> 1, half = ptid & 1;
         const float* trow = amat + t * kAStride;
         uint8_t* ts = sm + L::tstk;
-#pragma unroll
+#pragma unroll 1
         for (int c = 4 * half; c < 4 * half + 4; ++c) {
           uint32_t ww[4], hi[4], lo[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int m = 8 * c + 2 * e;
-            const float tb0 = trow[m] * vec[kC + m], tb1 = trow[m + 1] * vec[kC + m + 1];
-            const float tw0 = tb0 * fast_exp2(vec[m]), tw1 = tb1 * fast_exp2(vec[m + 1]);
+            const float tb0 = trow[m] * vec[V_BETA * kC + m], tb1 = trow[m + 1] * vec[V_BETA * kC + m + 1];
+            const float tw0 = tb0 * vec[V_EB * kC + m], tw1 = tb1 * vec[V_EB * kC + m + 1];
             ww[e] = Cvt<InT>::pack(tw0, tw1);
             hi[e] = Cvt<InT>::pack(tb0, tb1);
             const float2 hf = Cvt<InT>::unpack(hi[e]);
@@ -628,6 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[B_TREADY]);
+        if (ptid == 0) GDN_TR(10, i);
       }
       // W (fp32, TMEM lanes 0-63) -> fp16 rows 64-127 of Ahat[p] (or to global in prep-only mode)
       if (ok && ptid < 64) {
@@ -637,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
           tc_fence_after();
           const int t = ptid;
           uint8_t* ah = sm + (p ? L::ahat1 : L::ahat0);
-#pragma unroll
+#pragma unroll 1
           for (int c0 = 0; c0 < 128; c0 += 32) {
             float w[32];
             tmem_ld32w(tmem_addr(tmem + kTmW, wl * 32, c0), w);
@@ -663,14 +676,27 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
             mbar_arrive(&bars[B_WFREE]);
             if (!kPrepOnly) mbar_arrive(&bars[B_AFULL + p]);
           }
+          if (ptid == 0) GDN_TR(11, i);
         }
       }
     }
     if (!ok) *abort_flag = 1;
   } else {
     // ================================================================ chain
+    // Thread r owns row d = r of h^T (all BV columns of this slice) in fp32
+    // registers and TMEM lane r.  Per chunk:
+    //   D1 = [Qhat; W] h^T                 (issued by r = 0)
+    //   u  = U - W h^T      (rows 64-127 of D1 / the U accumulator)
+    //   D2 = Kbar^T u, D3 = P u            (issued by r = 64)
+    //   h  = e^{b_C} h + D2,  o = Qhat h^T + P u
+    // Named barriers carry the abort decision (bar.red.or), so every thread
+    // reaches the same barriers and leaves together.
     const int r = tid - 256;  // TMEM lane = state row d (0..127)
     const int wq = warp - 8;  // TMEM lane quarter of this warp
+    const uint32_t sb = smem_u32(sm);
+    const uint32_t id_1 = idesc_f16(128, BV, 0, 0, 1);
+    const uint32_t id_2 = idesc_f16(128, BV, 0, 1, 1);
+    const uint32_t id_3 = idesc_f16(128, BV, 0, 0, 1);
     float h[BV];
     const size_t hbase = (size_t(bb) * P.H + hh) * kV * kK;
     if (P.h0 != nullptr) {
@@ -681,15 +707,23 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
       for (int j = 0; j < BV; ++j) h[j] = 0.f;
     }
     bool ok = true;
-    if (!kPrepOnly) {
-      st_row16<BV>(sm + L::ht16, r, 0, h);
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_HFULL]);
-    }
-    for (int i = 0; i < NT && ok; ++i) {
-      const int p = i & 1;
-      if (kPrepOnly) {
+    // issue D1 for chunk c once h^T(c) is in shared memory (caller synchronised)
+    auto issue_d1 = [&](int c) -> bool {
+      if (!mbar_wait(&bars[B_AFULL + (c & 1)], (c >> 1) & 1, abort_flag)) return false;
+      tc_fence_after();
+      const uint32_t ab = sb + ((c & 1) ? L::ahat1 : L::ahat0);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_ss(tmem + TC::d1, sdesc(ab + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSw128),
+                   sdesc(sb + L::ht16 + kk * 2 * L::bv_sbo, 8192, L::bv_sbo, L::bv_swz), id_1, kk > 0);
+      mma_commit(&bars[B_D1]);
+      mma_commit(&bars[B_AFREE + (c & 1)]);
+      GDN_TR(3, c);
+      return true;
+    };
+    if (kPrepOnly) {
+      for (int i = 0; i < NT && ok; ++i) {
+        const int p = i & 1;
         if (r >= 64) {
           ok = mbar_wait_warp(&bars[B_UFULL + p], (i >> 1) & 1, abort_flag);
           if (!ok) break;
@@ -701,58 +735,90 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars[B_UFREE + p]);
         }
-        continue;
       }
-      ok = mbar_wait_warp(&bars[B_D1], i & 1, abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      float y[BV];
-      if (r >= 64) {
-        ok = mbar_wait_warp(&bars[B_UFULL + p], (i >> 1) & 1, abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-        float x[BV], uu[BV];
-        tmem_ld32w(tmem_addr(tmem + TC::d1, wq * 32, 0), x);
-        tmem_ld32w(tmem_addr(tmem + (p ? TC::u1 : TC::u0), wq * 32, 0), uu);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[B_UFREE + p]);
-#pragma unroll
-        for (int j = 0; j < BV; ++j) uu[j] -= x[j];  // u = U - W h^T   (gdn_ref.py:86)
-        st_row16<BV>(sm + L::u16, r - 64, 0, uu);
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[B_U16]);
-      } else {
-        tmem_ld32w(tmem_addr(tmem + TC::d1, wq * 32, 0), y);
-      }
-      ok = mbar_wait_warp(&bars[B_D2], i & 1, abort_flag) &&
-           mbar_wait_warp(&bars[B_VEC + (i & 3)], (i >> 2) & 1, abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      {
-        float dh[BV];
-        tmem_ld32w(tmem_addr(tmem + TC::d2, wq * 32, 0), dh);
-        const float gam = fast_exp2(vecs[(i & 3) * 2 * kC + kC - 1]);
-#pragma unroll
-        for (int j = 0; j < BV; ++j) h[j] = fmaf(gam, h[j], dh[j]);  // h' = e^{b_C} h + Kbar^T u
-      }
-      if (i + 1 < NT) st_row16<BV>(sm + L::ht16, r, 0, h);
-      {
-        float z[BV];
-        tmem_ld32w(tmem_addr(tmem + TC::d3, wq * 32, 0), z);
-        const int t = i * kC + r;
-        if (r < 64 && t < P.T) {
-#pragma unroll
-          for (int j = 0; j < BV; ++j) z[j] += y[j];  // o = Qhat h^T + P u   (gdn_ref.py:89-90)
-          OutT* dst = reinterpret_cast<OutT*>(P.o) + bb * P.so_b + (long long)t * P.so_t + hh * P.so_h + v0;
-          store_row<OutT>(dst, z, BV);
-        }
-      }
-      tc_fence_before();
+    } else {
+      st_row16<BV>(sm + L::ht16, r, 0, h);
       fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_HFULL]);
+      if (!bar_any(3, 128, false) && r == 0) {
+        if (!issue_d1(0)) *abort_flag = 1;
+      }
+      for (int i = 0; i < NT; ++i) {
+        const int p = i & 1;
+        ok = mbar_wait_warp(&bars[B_D1], i & 1, abort_flag);
+        if (ok) tc_fence_after();
+        if (ok && r == 0) GDN_TR(12, i);
+        float y[BV];
+        if (r >= 64) {
+          ok = ok && mbar_wait_warp(&bars[B_UFULL + p], (i >> 1) & 1, abort_flag);
+          if (ok) {
+            tc_fence_after();
+            float x[BV], uu[BV];
+            tmem_ld32w(tmem_addr(tmem + TC::d1, wq * 32, 0), x);
+            tmem_ld32w(tmem_addr(tmem + (p ? TC::u1 : TC::u0), wq * 32, 0), uu);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[B_UFREE + p]);
+#pragma unroll
+            for (int j = 0; j < BV; ++j) uu[j] -= x[j];  // u = U - W h^T   (gdn_ref.py:86)
+            st_row16<BV>(sm + L::u16, r - 64, 0, uu);
+            fence_async_smem();
+          }
+          if (r == 64) GDN_TR(13, i);
+          // D2 = Kbar^T u and D3 = P u, each accumulator's k-steps issued back to back
+          if (!bar_any(4, 64, !ok) && r == 64) {
+            if (mbar_wait(&bars[B_KFULL], i & 1, abort_flag) &&
+                mbar_wait(&bars[B_AFULL + p], (i >> 1) & 1, abort_flag)) {
+              tc_fence_after();
+              const uint32_t pb = sb + (p ? L::p1 : L::p0);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_f16_ss(tmem + TC::d2, sdesc(sb + L::kbar + kk * 2048, 8192, 1024, kSw128),
+                           sdesc(sb + L::u16 + kk * 2 * L::bv_sbo, 8192, L::bv_sbo, L::bv_swz), id_2, kk > 0);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_f16_ss(tmem + TC::d3, sdesc(pb + kk * 32, 16, 1024, kSw128),
+                           sdesc(sb + L::u16 + kk * 2 * L::bv_sbo, 8192, L::bv_sbo, L::bv_swz), id_3, kk > 0);
+              mma_commit(&bars[B_D2]);
+              mma_commit(&bars[B_KFREE]);
+              mma_commit(&bars[B_PFREE + p]);
+              GDN_TR(4, i);
+            } else {
+              *abort_flag = 1;
+            }
+          }
+        } else if (ok) {
+          tmem_ld32w(tmem_addr(tmem + TC::d1, wq * 32, 0), y);
+        }
+        ok = ok && mbar_wait_warp(&bars[B_D2], i & 1, abort_flag) &&
+             mbar_wait_warp(&bars[B_VEC + (i & 3)], (i >> 2) & 1, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          if (r == 0) GDN_TR(14, i);
+          float dh[BV];
+          tmem_ld32w(tmem_addr(tmem + TC::d2, wq * 32, 0), dh);
+          const float gam = vecs[(i & 3) * kVecN * kC + V_EB * kC + kC - 1];  // e^{b_C}
+#pragma unroll
+          for (int j = 0; j < BV; ++j) h[j] = fmaf(gam, h[j], dh[j]);  // h' = e^{b_C} h + Kbar^T u
+          if (i + 1 < NT) st_row16<BV>(sm + L::ht16, r, 0, h);
+          float z[BV];
+          tmem_ld32w(tmem_addr(tmem + TC::d3, wq * 32, 0), z);
+          const int t = i * kC + r;
+          if (r < 64 && t < P.T) {
+#pragma unroll
+            for (int j = 0; j < BV; ++j) z[j] += y[j];  // o = Qhat h^T + P u   (gdn_ref.py:89-90)
+            OutT* dst = reinterpret_cast<OutT*>(P.o) + bb * P.so_b + (long long)t * P.so_t + hh * P.so_h + v0;
+            store_row<OutT>(dst, z, BV);
+          }
+          tc_fence_before();
+          fence_async_smem();
+        }
+        if (bar_any(3, 128, !ok || *abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (r == 0) GDN_TR(15, i);
+        if (r == 0 && i + 1 < NT && !issue_d1(i + 1)) *abort_flag = 1;
+      }
     }
     if (ok && P.ht != nullptr) {
 #pragma unroll
@@ -864,6 +930,10 @@ int launch_out(const gdn_fwd_args* a, const FwdParams& p, int grid, cudaStream_t
   return GDN_ERR_INVALID_ARGUMENT;
 }
 
+#ifdef GDN_TRACE
+long long* g_trace = nullptr;
+#endif
+
 int run(const gdn_fwd_args* a, float* w_out, float* u_out, void* stream, bool prep) {
   const int rc = validate(a, !prep);
   if (rc != GDN_OK) return rc;
@@ -885,6 +955,9 @@ int run(const gdn_fwd_args* a, float* w_out, float* u_out, void* stream, bool pr
   p.w_out = w_out;
   p.u_out = u_out;
   p.status = a->status;
+#ifdef GDN_TRACE
+  p.trace = g_trace;
+#endif
   p.sb_b = a->beta_stride[0];
   p.sb_t = a->beta_stride[1];
   p.sb_h = a->beta_stride[2];
@@ -931,3 +1004,8 @@ extern "C" const char* gdn_status_string(int code) {
 }
 
 extern "C" int gdn_abi_version(void) { return GDN_B200_ABI_VERSION; }
+
+#ifdef GDN_TRACE
+// Trace builds only: device buffer of NT * 16 int64 timestamps for CTA 0.
+extern "C" void gdn_set_trace_buffer(long long* buf) { gdn::g_trace = buf; }
+#endif

@@ -12,8 +12,11 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
-#ifndef GDN_WAIT_TIMEOUT_NS
-#define GDN_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: far above any legitimate wait
+// Wait bound in SM clock cycles (~2 s at 2 GHz): far above any legitimate
+// wait.  clock64() is used instead of %globaltimer because it is a cheap
+// per-SM register read, so polling loops stay tight.
+#ifndef GDN_WAIT_TIMEOUT_CYCLES
+#define GDN_WAIT_TIMEOUT_CYCLES 4000000000ll
 #endif
 
 namespace gdn {
@@ -67,12 +70,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((it & 63u) == 0) {
+    if ((it & 15u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer() - t0 > GDN_WAIT_TIMEOUT_NS) {
+      if (clock64() - t0 > GDN_WAIT_TIMEOUT_CYCLES) {
         *abort_flag = 1;
         return false;
       }
@@ -200,6 +203,22 @@ __device__ __forceinline__ void tmem_ld32w(uint32_t taddr, float* v) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 16-column variant of tmem_ld32w.
+__device__ __forceinline__ void tmem_ld16w(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // Barrier `id` over `nthreads` threads that also ORs a predicate across them:
