@@ -56,7 +56,7 @@ def l2norm(x: np.ndarray, eps: float = 1e-6) -> np.ndarray:
 
 
 def _as(x, dtype):
-    return np.asarray(x, dtype=np.float32).astype(dtype)
+    return np.asarray(x).astype(dtype)
 
 
 def recurrent(q, k, v, beta, g, initial_state=None, dtype=np.float64):
@@ -173,14 +173,11 @@ def pad_to_multiple(q, k, v, beta, g, C):
     return padt(q), padt(k), padt(v), padt(beta), padt(g)
 
 
-def make_inputs(B, T, H, K, V, seed=0, gate_mean=0.0, h0_std=None,
-                in_dtype=np.float32):
-    """Seeded synthetic inputs with the BASELINE distributions.
+def make_inputs(B, T, H, K, V, seed=0, gate_mean=0.0, h0_std=None):
+    """Seeded synthetic float32 inputs with the BASELINE distributions.
 
     q, k = l2norm(N(0,1)) along K; v = N(0,1); beta = sigmoid(N(0,1));
     g = logsigmoid(N(gate_mean, 1)); h0 = N(0, h0_std) or None.
-    q/k/v are returned already rounded to ``in_dtype`` (held as float32 when
-    in_dtype is a 16-bit type numpy lacks; see ``round_to``).
     """
     rng = np.random.default_rng(seed)
     q = l2norm(rng.standard_normal((B, T, H, K), dtype=np.float32))

@@ -1,0 +1,169 @@
+"""GPU parity at the BASELINE configs' full sizes and the edge cases.
+
+The oracle (oracle/gdn_oracle.py, fp64) runs on exactly the 16-bit-rounded
+device inputs.  Where the full problem is too large for the CPU oracle, it is
+checked on a sample of (b, h) pairs -- every pair is an independent
+recurrence -- and through size-independent properties (state chaining,
+causality, memory independent of T).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import STORE_ROUNDING, TOL, make, oracle, rel
+from oracle import gdn_oracle as ora
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def gdn():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import gdn_b200
+    return gdn_b200
+
+
+def sampled_oracle(qd, kd, vd, bd, gd, h0, pairs, C=64):
+    """fp64 chunked oracle restricted to the listed (b, h) pairs."""
+    f = lambda x: x.float().cpu().numpy()
+    outs = []
+    for b, h in pairs:
+        sl = lambda x: f(x[b:b + 1, :, h:h + 1])
+        q, k, v, be, g = ora.pad_to_multiple(sl(qd), sl(kd), sl(vd), sl(bd), sl(gd), C)
+        hh = None if h0 is None else f(h0[b:b + 1, h:h + 1])
+        o, hs = ora.chunked(q, k, v, be, g, C=C, initial_state=hh)
+        outs.append((o[:, : qd.shape[1]], hs))
+    return outs
+
+
+def check_pairs(o, ht, refs, pairs, out_tol):
+    for (b, h), (o_ref, h_ref) in zip(pairs, refs):
+        assert rel(o[b:b + 1, :, h:h + 1], o_ref) < out_tol, (b, h)
+        assert rel(ht[b:b + 1, h:h + 1], h_ref) < TOL, (b, h)
+
+
+def test_config1_full_fp16(gdn):
+    """B2 T2048 H8 K=V=128 fp16, h0 = 0, against the fp64 step recurrence."""
+    qd, kd, vd, bd, gd, _ = make(2, 2048, 8, seed=21, dtype=torch.float16)
+    o, ht = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, check=True)
+    o_ref, h_ref = oracle(qd, kd, vd, bd, gd, None)
+    assert rel(o, o_ref) < TOL + STORE_ROUNDING[torch.float16]
+    assert rel(ht, h_ref) < TOL
+
+
+def test_config2_full_bf16(gdn):
+    """Headline shape B2 T4096 H16 bf16 with h0 ~ N(0, 0.1): fp32 output meets 1e-3."""
+    qd, kd, vd, bd, gd, h0 = make(2, 4096, 16, seed=22, dtype=torch.bfloat16, h0_std=0.1)
+    o, ht = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
+    o_ref, h_ref = oracle(qd, kd, vd, bd, gd, h0, chunked=True)
+    assert rel(o, o_ref) < TOL
+    assert rel(ht, h_ref) < TOL
+    o16, ht16 = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, check=True)
+    assert rel(o16, o_ref) < TOL + STORE_ROUNDING[torch.bfloat16]
+    assert torch.equal(ht16, ht)  # the state never passes through the output dtype
+
+
+@pytest.mark.parametrize("T", [16384, 65536])
+def test_config3_long_sequence(gdn, T):
+    """B2 H16 bf16, slow decay g = logsigmoid(N(2,1)); sampled heads against the oracle."""
+    qd, kd, vd, bd, gd, _ = make(2, T, 16, seed=23, dtype=torch.bfloat16, gate_mean=2.0)
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    o, ht = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, output_dtype=torch.float32, check=True)
+    peak_extra = torch.cuda.max_memory_allocated() - base
+    out_bytes = o.numel() * 4 + ht.numel() * 4
+    # O(B*H*K*V) state memory: nothing beyond the outputs is allocated, at any T
+    assert peak_extra <= out_bytes + 4096
+    pairs = [(0, 0), (1, 15)]
+    check_pairs(o, ht, sampled_oracle(qd, kd, vd, bd, gd, None, pairs), pairs, TOL)
+
+
+def test_config4_sampled_heads(gdn):
+    """B8 T8192 H32 bf16 with h0: the sharded config run on one GPU, sampled pairs."""
+    qd, kd, vd, bd, gd, h0 = make(8, 8192, 32, seed=24, dtype=torch.bfloat16, h0_std=0.1)
+    o, ht = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
+    pairs = [(0, 0), (3, 17), (7, 31)]
+    check_pairs(o, ht, sampled_oracle(qd, kd, vd, bd, gd, h0, pairs), pairs, TOL)
+
+
+def test_state_chaining_across_calls(gdn):
+    """Running T in two calls with the state passed equals one call."""
+    qd, kd, vd, bd, gd, h0 = make(1, 1000, 4, seed=25, dtype=torch.bfloat16, h0_std=0.1)
+    o, ht = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
+    cut = 448
+    oa, ha = gdn.gdn_chunk_fwd(qd[:, :cut], kd[:, :cut], vd[:, :cut], bd[:, :cut], gd[:, :cut],
+                               initial_state=h0, output_dtype=torch.float32, check=True)
+    ob, hb = gdn.gdn_chunk_fwd(qd[:, cut:], kd[:, cut:], vd[:, cut:], bd[:, cut:], gd[:, cut:],
+                               initial_state=ha, output_dtype=torch.float32, check=True)
+    o_ref, h_ref = oracle(qd, kd, vd, bd, gd, h0)
+    assert rel(torch.cat([oa, ob], 1), o_ref) < TOL
+    assert rel(hb, h_ref) < TOL
+    assert rel(o, o_ref) < TOL
+
+
+@pytest.mark.parametrize("T", [1, 31, 63, 65, 130])
+def test_ragged_and_tiny_T(gdn, T):
+    qd, kd, vd, bd, gd, h0 = make(1, T, 2, seed=26 + T, dtype=torch.float16, h0_std=0.1)
+    o, ht = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
+    o_ref, h_ref = oracle(qd, kd, vd, bd, gd, h0)
+    assert o.shape == (1, T, 2, 128)
+    assert rel(o, o_ref) < TOL and rel(ht, h_ref) < TOL
+
+
+def test_zero_state_equals_no_state(gdn):
+    qd, kd, vd, bd, gd, _ = make(1, 192, 3, seed=31, dtype=torch.bfloat16)
+    z = torch.zeros(1, 3, 128, 128, device="cuda")
+    o1, h1 = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, check=True)
+    o2, h2 = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=z, check=True)
+    assert torch.equal(o1, o2) and torch.equal(h1, h2)
+
+
+def test_strided_head_views(gdn):
+    """Inputs that are head slices of wider tensors (the multi-GPU shard views)."""
+    qd, kd, vd, bd, gd, h0 = make(2, 256, 6, seed=32, dtype=torch.bfloat16, h0_std=0.1)
+    sl = lambda x: x[:, :, 2:5]
+    o, ht = gdn.gdn_chunk_fwd(sl(qd), sl(kd), sl(vd), sl(bd), sl(gd), initial_state=h0[:, 2:5],
+                              output_dtype=torch.float32, check=True)
+    o_ref, h_ref = oracle(sl(qd), sl(kd), sl(vd), sl(bd), sl(gd), h0[:, 2:5])
+    assert rel(o, o_ref) < TOL and rel(ht, h_ref) < TOL
+
+
+def test_reference_distribution(gdn):
+    """The reference's own test inputs: beta ~ U(0.4, 0.9), g ~ -U(0, s) (bench_gdn.py:33-40)."""
+    torch.manual_seed(0)
+    B, T, H = 2, 256, 4
+    for s in (0.05, 0.3):
+        q = torch.nn.functional.normalize(torch.randn(B, T, H, 128), dim=-1).half().cuda()
+        k = torch.nn.functional.normalize(torch.randn(B, T, H, 128), dim=-1).half().cuda()
+        v = torch.randn(B, T, H, 128).half().cuda()
+        beta = (torch.rand(B, T, H) * 0.5 + 0.4).cuda()
+        g = (-torch.rand(B, T, H) * s).cuda()
+        o, ht = gdn.gdn_chunk_fwd(q, k, v, beta, g, check=True)
+        o_ref, h_ref = oracle(q, k, v, beta, g, None)
+        assert rel(o, o_ref) < TOL + STORE_ROUNDING[torch.float16]
+        assert rel(ht, h_ref) < TOL
+
+
+def test_v2_entry_point(gdn):
+    qd, kd, vd, bd, gd, _ = make(1, 128, 2, seed=33, dtype=torch.float16)
+    o1, h1 = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, check=True)
+    o2, h2 = gdn.gdn_chunk_fwd_v2(qd, kd, vd, bd, gd, C=64, BV=32, num_warps=4, num_stages=1, iters=2)
+    assert torch.equal(o1, o2) and torch.equal(h1, h2)
+
+
+def test_unsupported_requests_raise(gdn):
+    qd, kd, vd, bd, gd, _ = make(1, 64, 1, seed=34, dtype=torch.float16)
+    with pytest.raises(NotImplementedError):
+        gdn.gdn_chunk_fwd(qd.float(), kd.float(), vd.float(), bd, gd)
+    with pytest.raises(NotImplementedError):
+        gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, chunk_size=32)
+
+
+def test_repeat_calls_deterministic(gdn):
+    qd, kd, vd, bd, gd, h0 = make(1, 320, 2, seed=35, dtype=torch.bfloat16, h0_std=0.1)
+    a = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, check=True)
+    b = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, check=True)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])

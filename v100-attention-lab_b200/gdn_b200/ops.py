@@ -63,12 +63,6 @@ def _check_inputs(q, k, v, beta, g):
     for name, t in tensors.items():
         if not isinstance(t, torch.Tensor):
             raise TypeError(f"{name} must be a torch.Tensor")
-        if not t.is_cuda:
-            raise ValueError(f"{name} must be a CUDA tensor (got device {t.device})")
-    dev = q.device
-    for name, t in tensors.items():
-        if t.device != dev:
-            raise ValueError(f"{name} is on {t.device}, q is on {dev}")
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         raise ValueError("q, k, v must be [B, T, H, K] / [B, T, H, V]")
     B, T, H, K = q.shape
@@ -85,6 +79,12 @@ def _check_inputs(q, k, v, beta, g):
     for name in ("q", "k", "v"):
         if tensors[name].stride(-1) != 1:
             raise ValueError(f"{name} must have a contiguous last dimension")
+    dev = q.device
+    for name, t in tensors.items():
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor (got device {t.device})")
+        if t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, q is on {dev}")
     return B, T, H, K, v.shape[-1]
 
 
