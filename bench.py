@@ -67,6 +67,18 @@ def load_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def measured_traffic(config):
+    """DRAM bytes per launch from the committed ncu summary, if one covers this config."""
+    path = os.path.join(ROOT, "profiles", f"gdn_fwd_config{config}_traffic.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 def algo_bytes(B, T, H, s_in=2, s_out=2, h0=True):
     """Algorithmic HBM bytes of one forward: q,k,v read, o written, beta/g read,
     h0 read (if given) and the final state written."""
@@ -354,7 +366,8 @@ def run_ours(args, cfg, rank, world, local):
                    "l2": f"inputs rotate over {nsets} resident sets ({nsets * in_bytes_one / 1e6:.0f} MB > 2x L2)",
                    "parallelism": f"{world} GPU(s), disjoint (batch, head) shards, no collective"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "traffic": None, "peak_source": peak_src, "algorithmic_bytes_per_launch": abytes,
+                     "traffic": measured_traffic(args.config) if world == 1 else None,
+                     "peak_source": peak_src, "algorithmic_bytes_per_launch": abytes,
                      "tensor_frac": flops / kern_s / 1e12 / tf},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": steps,

@@ -101,6 +101,16 @@ int gdn_fwd_sm100(const gdn_fwd_args* args, void* stream);
  */
 int gdn_wy_prep_sm100(const gdn_fwd_args* args, float* W, float* U, void* stream);
 
+/*
+ * Diagnostic of the device-side failure detection: launches one CTA that
+ * waits on an mbarrier nothing ever arrives at, with the bounded wait every
+ * kernel of this library uses, limited to `limit_cycles` SM clock cycles.
+ * When the limit expires the kernel ORs (1 << GDN_ERR_TIMEOUT) into *status
+ * (a device int) and exits, leaving the context usable.  No counterpart in
+ * the reference, whose kernels have no device-side waits.
+ */
+int gdn_selftest_wait_timeout(int* status, long long limit_cycles, void* stream);
+
 /* Human-readable text of a gdn_status code. */
 const char* gdn_status_string(int code);
 

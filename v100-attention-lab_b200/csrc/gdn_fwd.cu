@@ -982,6 +982,31 @@ int run(const gdn_fwd_args* a, float* w_out, float* u_out, void* stream, bool pr
 }  // namespace
 }  // namespace gdn
 
+namespace gdn {
+// Diagnostic: one CTA waits on an mbarrier that nothing arrives at, through
+// the same bounded wait the forward kernel uses, and reports the expiry.
+__global__ void wait_timeout_probe_kernel(int* status, long long limit_cycles) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool ok = mbar_wait_warp(&bar, 0, &abort_flag, limit_cycles);
+  if (!ok && threadIdx.x == 0) atomicOr(status, 1 << GDN_ERR_TIMEOUT);
+}
+}  // namespace gdn
+
+extern "C" int gdn_selftest_wait_timeout(int* status, long long limit_cycles, void* stream) {
+  if (status == nullptr || limit_cycles <= 0) return GDN_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  if (!gdn::device_is_sm100(&dev)) return GDN_ERR_NO_DEVICE;
+  gdn::wait_timeout_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, limit_cycles);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}
+
 extern "C" int gdn_fwd_sm100(const gdn_fwd_args* args, void* stream) {
   return gdn::run(args, nullptr, nullptr, stream, false);
 }

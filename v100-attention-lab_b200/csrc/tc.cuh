@@ -67,7 +67,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Bounded wait for phase `parity` of `bar`.  Returns false (and raises the
 // CTA abort flag) on timeout or when another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          long long limit_cycles = GDN_WAIT_TIMEOUT_CYCLES) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long t0 = clock64();
@@ -75,7 +76,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(a, parity)) return true;
     if ((it & 15u) == 0) {
       if (*abort_flag) return false;
-      if (clock64() - t0 > GDN_WAIT_TIMEOUT_CYCLES) {
+      if (clock64() - t0 > limit_cycles) {
         *abort_flag = 1;
         return false;
       }
@@ -85,8 +86,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 
 // Warp-uniform bounded wait: every lane returns the same result, so the
 // .sync.aligned instructions that follow are executed by the whole warp.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  const bool ok = mbar_wait(bar, parity, abort_flag);
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               long long limit_cycles = GDN_WAIT_TIMEOUT_CYCLES) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, limit_cycles);
   return __all_sync(0xffffffffu, ok);
 }
 

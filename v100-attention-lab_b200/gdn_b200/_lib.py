@@ -27,7 +27,8 @@ ERR_TIMEOUT = 5
 ERR_NO_DEVICE = 6
 
 # Every symbol include/gdn_b200.h declares.
-EXPORTED_SYMBOLS = ("gdn_fwd_sm100", "gdn_wy_prep_sm100", "gdn_status_string", "gdn_abi_version")
+EXPORTED_SYMBOLS = ("gdn_fwd_sm100", "gdn_wy_prep_sm100", "gdn_selftest_wait_timeout", "gdn_status_string",
+                    "gdn_abi_version")
 
 _i64x3 = ctypes.c_int64 * 3
 
@@ -95,6 +96,8 @@ def load(build_if_missing: bool = False) -> ctypes.CDLL:
         lib.gdn_wy_prep_sm100.argtypes = [ctypes.POINTER(GdnFwdArgs), ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_void_p]
         lib.gdn_wy_prep_sm100.restype = ctypes.c_int
+        lib.gdn_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p]
+        lib.gdn_selftest_wait_timeout.restype = ctypes.c_int
         lib.gdn_status_string.argtypes = [ctypes.c_int]
         lib.gdn_status_string.restype = ctypes.c_char_p
         lib.gdn_abi_version.argtypes = []
