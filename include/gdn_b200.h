@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define GDN_B200_ABI_VERSION 1
+#define GDN_B200_ABI_VERSION 2
 
 /* Element types (q/k/v inputs, o output). */
 enum gdn_dtype {
@@ -81,16 +81,33 @@ typedef struct gdn_fwd_args {
   int64_t o_stride[3];
   float* ht;
   int32_t* status; /* optional device int; the kernel ORs error bits into it */
+  /* Scratch for the two-kernel path (see gdn_fwd_workspace_bytes).  NULL or
+   * too small for one chunk per (b, h): the single fused kernel runs instead. */
+  void* workspace;
+  uint64_t workspace_bytes;
 } gdn_fwd_args;
 
 /*
- * Launch the fused chunked GDN forward on `stream` (a cudaStream_t; NULL is
- * the legacy default stream).  Asynchronous: returns after the launch.
+ * Launch the chunked GDN forward on `stream` (a cudaStream_t; NULL is the
+ * legacy default stream).  Asynchronous: returns after the launch(es).
  * Replaces gdn_chunk_fwd (gdn_triton.py:113) / gdn_chunk_fwd_v2
  * (gdn_triton_v2.py:92); the caller owns and allocates o and ht, as the
  * reference allocates them inside its wrapper (gdn_triton.py:126-127).
+ *
+ * With a workspace it runs two kernels per segment of chunks: the
+ * chunk-parallel WY/UT preparation (40 KB of operands per (b, h, chunk) in the
+ * workspace) and the state scan; segments are sized to the workspace and the
+ * state is carried between them.  Without one it runs the single fused kernel.
  */
 int gdn_fwd_sm100(const gdn_fwd_args* args, void* stream);
+
+/*
+ * Workspace bytes that let gdn_fwd_sm100 run the whole sequence as one
+ * segment: B*H*ceil(T/C)*40960 + B*H*V*K*4 (state carried between segments).
+ * Any smaller workspace of at least B*H*(40960 + V*K*4) bytes works with more
+ * segments.  Returns 0 for invalid arguments.
+ */
+uint64_t gdn_fwd_workspace_bytes(const gdn_fwd_args* args);
 
 /*
  * Chunk-parallel WY/UT preparation only (the per-chunk, state-independent

@@ -21,7 +21,7 @@ def lib():
 
 def declared_functions():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*|void)\s+(gdn_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*|void|uint64_t)\s+(gdn_\w+)\s*\(", text, re.M)))
 
 
 def test_header_declares_expected_entry_points():
@@ -103,3 +103,12 @@ def test_valid_args_without_sm100_report_no_device(lib):
 
 def test_null_args_pointer(lib):
     assert lib.gdn_fwd_sm100(None, None) == 1
+
+
+def test_workspace_query(lib):
+    a = _args(B=2, T=4096, H=16)
+    # one 40 KB packet per (b, h, chunk) plus one fp32 state per (b, h)
+    assert lib.gdn_fwd_workspace_bytes(ctypes.byref(a)) == 2 * 16 * (64 * 40960 + 128 * 128 * 4)
+    a = _args(T=100)
+    assert lib.gdn_fwd_workspace_bytes(ctypes.byref(a)) == 1 * 1 * (2 * 40960 + 128 * 128 * 4)
+    assert lib.gdn_fwd_workspace_bytes(None) == 0

@@ -20,12 +20,14 @@ def gdn():
     return gdn_b200
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("T", [64, 128, 200])
 @pytest.mark.parametrize("with_h0", [False, True])
-def test_small_fp32_out(gdn, dtype, T, with_h0):
+def test_small_fp32_out(gdn, dtype, T, with_h0, fused):
     qd, kd, vd, bd, gd, h0 = make(1, T, 2, seed=T + with_h0, dtype=dtype, h0_std=0.1 if with_h0 else None)
-    o, ht = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
+    o, ht = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True,
+                              fused=fused)
     o_ref, h_ref = oracle(qd, kd, vd, bd, gd, h0)
     assert rel(o, o_ref) < TOL
     assert rel(ht, h_ref) < TOL
@@ -56,3 +58,34 @@ def test_wy_prep_stage(gdn):
                               b[:, sl].transpose(0, 2, 1), g[:, sl].transpose(0, 2, 1))
         assert ora.max_rel(f(W[:, :, c]), st["W"]) < 5e-3   # W uses input-dtype operands
         assert ora.max_rel(f(U[:, :, c]), st["U"]) < 1e-4   # U uses the hi+lo split
+
+
+def test_two_kernel_matches_fused(gdn):
+    """The two paths compute the same operands; results agree to fp32 rounding."""
+    qd, kd, vd, bd, gd, h0 = make(2, 700, 3, seed=41, dtype=torch.bfloat16, h0_std=0.1)
+    o1, h1 = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
+    o2, h2 = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True,
+                               fused=True)
+    assert rel(o1, o2.float().cpu().numpy()) < 1e-5
+    assert rel(h1, h2.float().cpu().numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("cap_chunks", [1, 3])
+def test_segmented_workspace(gdn, cap_chunks, monkeypatch):
+    """A workspace smaller than the sequence: several prep/scan segments with
+    the state carried between them."""
+    from gdn_b200 import ops
+    B, H = 1, 2
+    cap = B * H * (cap_chunks * 40960 + 128 * 128 * 4)
+    monkeypatch.setattr(ops, "WORKSPACE_CAP_BYTES", cap)
+    monkeypatch.setattr(ops, "_workspaces", {})
+    qd, kd, vd, bd, gd, h0 = make(B, 450, H, seed=42, dtype=torch.float16, h0_std=0.1)
+    for want_state in (True, False):
+        o, ht = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32,
+                                  output_final_state=want_state, check=True)
+        o_ref, h_ref = oracle(qd, kd, vd, bd, gd, h0)
+        assert rel(o, o_ref) < TOL
+        if want_state:
+            assert rel(ht, h_ref) < TOL
+        else:
+            assert ht is None

@@ -32,8 +32,9 @@
 // (D1, D2, D3) take fp16 operands with fp32 accumulation, the same choice the
 // reference makes for its state casts (gdn_triton.py:87, :93-94, :101-106).
 // The state itself stays fp32 for the whole sequence.
-#include "tc.cuh"
+#include "gdn_common.cuh"
 #include "tmap.h"
+#include "gdn_wy_scan.h"
 #include "../../include/gdn_b200.h"
 
 #include <cuda_runtime.h>
@@ -42,13 +43,7 @@
 
 namespace gdn {
 
-constexpr int kC = 64;    // chunk length
-constexpr int kK = 128;   // key dim
-constexpr int kV = 128;   // value dim
 constexpr int kThreads = 384;
-constexpr int kAStride = 68;  // fp32 row stride of the A/T work matrix (column 64 holds F_m)
-constexpr int kVecN = 4;      // per-chunk vectors: b*log2(e) (cumsum), beta, e^b, e^(b_C - b)
-enum : int { V_B2 = 0, V_BETA = 1, V_EB = 2, V_DD = 3 };
 
 // ------------------------------------------------------------------ layout
 template <int BV>
@@ -134,176 +129,6 @@ struct FwdParams {
   long long so_b, so_t, so_h;
   int B, T, H, NT, nslice;
 };
-
-// Tracing: with -DGDN_TRACE the kernel records clock64() at fixed points of
-// each role for every chunk of CTA 0 into P.trace[chunk * kTraceSlots + slot].
-constexpr int kTraceSlots = 24;
-#ifdef GDN_TRACE
-#define GDN_TR(slot, chunk)                                                                  \
-  do {                                                                                       \
-    if (P.trace != nullptr && blockIdx.x == 0) P.trace[(chunk) * kTraceSlots + (slot)] = clock64(); \
-  } while (0)
-#else
-#define GDN_TR(slot, chunk) \
-  do {                      \
-  } while (0)
-#endif
-
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-template <typename OutT>
-__device__ __forceinline__ void store_row(OutT* dst, const float* v, int n);
-
-template <>
-__device__ __forceinline__ void store_row<float>(float* dst, const float* v, int n) {
-  for (int i = 0; i < n; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-}
-template <>
-__device__ __forceinline__ void store_row<__half>(__half* dst, const float* v, int n) {
-  for (int i = 0; i < n; i += 8) {
-    uint4 w;
-    w.x = Cvt<__half>::pack(v[i], v[i + 1]);
-    w.y = Cvt<__half>::pack(v[i + 2], v[i + 3]);
-    w.z = Cvt<__half>::pack(v[i + 4], v[i + 5]);
-    w.w = Cvt<__half>::pack(v[i + 6], v[i + 7]);
-    *reinterpret_cast<uint4*>(dst + i) = w;
-  }
-}
-template <>
-__device__ __forceinline__ void store_row<__nv_bfloat16>(__nv_bfloat16* dst, const float* v, int n) {
-  for (int i = 0; i < n; i += 8) {
-    uint4 w;
-    w.x = Cvt<__nv_bfloat16>::pack(v[i], v[i + 1]);
-    w.y = Cvt<__nv_bfloat16>::pack(v[i + 2], v[i + 3]);
-    w.z = Cvt<__nv_bfloat16>::pack(v[i + 4], v[i + 5]);
-    w.w = Cvt<__nv_bfloat16>::pack(v[i + 6], v[i + 7]);
-    *reinterpret_cast<uint4*>(dst + i) = w;
-  }
-}
-
-// Write 32 fp32 values as fp16 into row r of a BV=32 (64-byte rows, SW64) or
-// the first half of a BV=64 (128-byte rows, SW128) MN-major tile.
-template <int BV>
-__device__ __forceinline__ void st_row16(uint8_t* tile, uint32_t r, uint32_t c16_base, const float* v) {
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint4 w;
-    w.x = Cvt<__half>::pack(v[8 * c + 0], v[8 * c + 1]);
-    w.y = Cvt<__half>::pack(v[8 * c + 2], v[8 * c + 3]);
-    w.z = Cvt<__half>::pack(v[8 * c + 4], v[8 * c + 5]);
-    w.w = Cvt<__half>::pack(v[8 * c + 6], v[8 * c + 7]);
-    const uint32_t off = (BV == 32) ? sw64_off(r, c16_base + c) : sw128_off(r, c16_base + c);
-    *reinterpret_cast<uint4*>(tile + off) = w;
-  }
-}
-
-// ------------------------------------------------------------------ the inverse
-// T = (I + A)^-1 for the 64x64 strictly-lower A held in `am` (row stride
-// kAStride), in place, by the 128 prep threads (named barrier 1).  Eight 8x8
-// diagonal blocks are inverted by column forward substitution; three
-// doubling levels (8 -> 16 -> 32 -> 64) then apply
-//     inv([[L0, 0], [X, L1]]) = [[inv(L0), 0], [-inv(L1) X inv(L0), inv(L1)]].
-// The upper triangle of every block stays zero, so the block products can run
-// over full index ranges.  Same result as the row-by-row forward substitution
-// of gdn_triton.py:75-84 applied to the identity.
-template <int N>
-__device__ __forceinline__ void inv_level(float* am, int tid) {
-  constexpr int NTH = 128;
-  constexpr int NOUT = (64 / (2 * N)) * N * N;  // outputs per phase
-  constexpr int PER = NOUT / NTH;               // outputs per thread
-  float acc[PER];
-  // phase 1: Y = X inv(L0), X = rows N..2N-1 x cols 0..N-1 of each 2N block
-#pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NTH;
-    const int pr = idx / (N * N), rem = idx % (N * N);
-    const int i = rem / N, j = rem % N, o = pr * 2 * N;
-    const float* xr = am + (o + N + i) * kAStride + o;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-    for (int m = 0; m < N; m += 4) {
-      const float4 xv = *reinterpret_cast<const float4*>(xr + m);
-      s0 = fmaf(xv.x, am[(o + m + 0) * kAStride + o + j], s0);
-      s1 = fmaf(xv.y, am[(o + m + 1) * kAStride + o + j], s1);
-      s2 = fmaf(xv.z, am[(o + m + 2) * kAStride + o + j], s2);
-      s3 = fmaf(xv.w, am[(o + m + 3) * kAStride + o + j], s3);
-    }
-    acc[e] = (s0 + s1) + (s2 + s3);
-  }
-  named_bar(1, NTH);
-#pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NTH;
-    const int pr = idx / (N * N), rem = idx % (N * N);
-    am[(pr * 2 * N + N + rem / N) * kAStride + pr * 2 * N + rem % N] = acc[e];
-  }
-  named_bar(1, NTH);
-  // phase 2: T = -inv(L1) Y
-#pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NTH;
-    const int pr = idx / (N * N), rem = idx % (N * N);
-    const int i = rem / N, j = rem % N, o = pr * 2 * N;
-    const float* tr = am + (o + N + i) * kAStride + o + N;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-    for (int p = 0; p < N; p += 4) {
-      const float4 tv = *reinterpret_cast<const float4*>(tr + p);
-      s0 = fmaf(tv.x, am[(o + N + p + 0) * kAStride + o + j], s0);
-      s1 = fmaf(tv.y, am[(o + N + p + 1) * kAStride + o + j], s1);
-      s2 = fmaf(tv.z, am[(o + N + p + 2) * kAStride + o + j], s2);
-      s3 = fmaf(tv.w, am[(o + N + p + 3) * kAStride + o + j], s3);
-    }
-    acc[e] = -((s0 + s1) + (s2 + s3));
-  }
-  named_bar(1, NTH);
-#pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NTH;
-    const int pr = idx / (N * N), rem = idx % (N * N);
-    am[(pr * 2 * N + N + rem / N) * kAStride + pr * 2 * N + rem % N] = acc[e];
-  }
-  named_bar(1, NTH);
-}
-
-__device__ __forceinline__ void invert_unit_lower64(float* am, int ptid) {
-  if (ptid < 64) {
-    const int blk_id = ptid >> 3, c = ptid & 7;
-    float* blk = am + (8 * blk_id) * kAStride + 8 * blk_id;
-    float x[8];
-#pragma unroll
-    for (int m = 0; m < 8; ++m) x[m] = (m == c) ? 1.f : 0.f;
-#pragma unroll
-    for (int t = 1; t < 8; ++t) {
-      float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-      for (int m = 0; m < t; ++m) {
-        if (m & 1)
-          a1 = fmaf(blk[t * kAStride + m], x[m], a1);
-        else
-          a0 = fmaf(blk[t * kAStride + m], x[m], a0);
-      }
-      if (t > c) x[t] = -(a0 + a1);
-    }
-    __syncwarp();
-#pragma unroll
-    for (int t = 0; t < 8; ++t) blk[t * kAStride + c] = x[t];
-  }
-  named_bar(1, 128);
-  inv_level<8>(am, ptid);
-  inv_level<16>(am, ptid);
-  inv_level<32>(am, ptid);
-}
 
 // ------------------------------------------------------------------ kernel
 // Abort protocol: every wait is bounded (tc.cuh).  A role that gives up sets
@@ -934,6 +759,62 @@ int launch_out(const gdn_fwd_args* a, const FwdParams& p, int grid, cudaStream_t
 long long* g_trace = nullptr;
 #endif
 
+// Two-kernel path: per segment of chunks, the WY/UT prep kernel writes one
+// packet per (b, h, chunk) into the workspace and the scan kernel consumes
+// them; the state is carried between segments through ht (or the
+// workspace's state area when the caller does not want ht).
+int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint64_t state_bytes) {
+  constexpr int BV = 32;
+  const int NT = (a->T + kC - 1) / kC;
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  float* state = a->ht != nullptr ? a->ht : reinterpret_cast<float*>(ws);
+  uint8_t* packets = ws + state_bytes;
+  const int ns_max = int((a->workspace_bytes - state_bytes) / per_chunk);
+  WyParams wp;
+  ScanParams sp;
+  memset(&wp, 0, sizeof(wp));
+  memset(&sp, 0, sizeof(sp));
+  if (!make_input_map(&wp.tm_q, a, a->q, a->q_stride, kK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_input_map(&wp.tm_k, a, a->k, a->k_stride, kK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_input_map(&sp.tm_v, a, a->v, a->v_stride, kV, BV, CU_TENSOR_MAP_SWIZZLE_64B))
+    return GDN_ERR_CUDA;
+  sp.tm_q = wp.tm_q;
+  sp.tm_k = wp.tm_k;
+  wp.beta = sp.beta = a->beta;
+  wp.g = sp.g = a->g;
+  wp.status = sp.status = a->status;
+  wp.packets = packets;
+  sp.packets = packets;
+  wp.sb_b = sp.sb_b = a->beta_stride[0];
+  wp.sb_t = sp.sb_t = a->beta_stride[1];
+  wp.sb_h = sp.sb_h = a->beta_stride[2];
+  wp.sg_b = sp.sg_b = a->g_stride[0];
+  wp.sg_t = sp.sg_t = a->g_stride[1];
+  wp.sg_h = sp.sg_h = a->g_stride[2];
+  sp.so_b = a->o_stride[0];
+  sp.so_t = a->o_stride[1];
+  sp.so_h = a->o_stride[2];
+  sp.o = a->o;
+  sp.ht = state;
+  wp.B = sp.B = a->B;
+  wp.T = sp.T = a->T;
+  wp.H = sp.H = a->H;
+  sp.nslice = kV / BV;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int in_bf16 = a->in_dtype == GDN_DTYPE_BF16;
+  for (int c0 = 0; c0 < NT; c0 += ns_max) {
+    const int ns = (NT - c0 < ns_max) ? NT - c0 : ns_max;
+    wp.c0 = sp.c0 = c0;
+    wp.NS = sp.NS = ns;
+    sp.h0 = (c0 == 0) ? a->h0 : state;
+    int rc = run_wy(in_bf16, wp, a->B * a->H * ns, s);
+    if (rc != GDN_OK) return rc;
+    rc = run_scan(in_bf16, a->out_dtype, sp, a->B * a->H * sp.nslice, s);
+    if (rc != GDN_OK) return rc;
+  }
+  return GDN_OK;
+}
+
 int run(const gdn_fwd_args* a, float* w_out, float* u_out, void* stream, bool prep) {
   const int rc = validate(a, !prep);
   if (rc != GDN_OK) return rc;
@@ -941,6 +822,12 @@ int run(const gdn_fwd_args* a, float* w_out, float* u_out, void* stream, bool pr
   if (!device_is_sm100(&dev)) return GDN_ERR_NO_DEVICE;
   if (prep && (w_out == nullptr || u_out == nullptr)) return GDN_ERR_INVALID_ARGUMENT;
   constexpr int BV = 32;
+  if (!prep && a->workspace != nullptr) {
+    const uint64_t per_chunk = uint64_t(a->B) * a->H * kPacketBytesPerChunk;
+    const uint64_t state_bytes = uint64_t(a->B) * a->H * kV * kK * 4;
+    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0 && a->workspace_bytes >= state_bytes + per_chunk)
+      return run_two_kernel(a, stream, per_chunk, state_bytes);
+  }
   FwdParams p;
   memset(&p, 0, sizeof(p));
   if (!make_input_map(&p.tm_q, a, a->q, a->q_stride, kK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1029,6 +916,12 @@ extern "C" const char* gdn_status_string(int code) {
 }
 
 extern "C" int gdn_abi_version(void) { return GDN_B200_ABI_VERSION; }
+
+extern "C" uint64_t gdn_fwd_workspace_bytes(const gdn_fwd_args* a) {
+  if (a == nullptr || a->B < 1 || a->H < 1 || a->T < 1 || a->chunk_size != gdn::kC) return 0;
+  const uint64_t nt = (uint64_t(a->T) + gdn::kC - 1) / gdn::kC;
+  return uint64_t(a->B) * a->H * (nt * gdn::kPacketBytesPerChunk + uint64_t(gdn::kV) * gdn::kK * 4);
+}
 
 #ifdef GDN_TRACE
 // Trace builds only: device buffer of NT * 16 int64 timestamps for CTA 0.

@@ -12,7 +12,7 @@ import threading
 
 from . import _build
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 DTYPE_F32 = 0
 DTYPE_F16 = 1
@@ -27,8 +27,8 @@ ERR_TIMEOUT = 5
 ERR_NO_DEVICE = 6
 
 # Every symbol include/gdn_b200.h declares.
-EXPORTED_SYMBOLS = ("gdn_fwd_sm100", "gdn_wy_prep_sm100", "gdn_selftest_wait_timeout", "gdn_status_string",
-                    "gdn_abi_version")
+EXPORTED_SYMBOLS = ("gdn_fwd_sm100", "gdn_fwd_workspace_bytes", "gdn_wy_prep_sm100", "gdn_selftest_wait_timeout",
+                    "gdn_status_string", "gdn_abi_version")
 
 _i64x3 = ctypes.c_int64 * 3
 
@@ -62,6 +62,8 @@ class GdnFwdArgs(ctypes.Structure):
         ("o_stride", _i64x3),
         ("ht", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_uint64),
     ]
 
 
@@ -93,6 +95,8 @@ def load(build_if_missing: bool = False) -> ctypes.CDLL:
             raise RuntimeError(f"gdn_b200: {path} lacks symbols {missing}")
         lib.gdn_fwd_sm100.argtypes = [ctypes.POINTER(GdnFwdArgs), ctypes.c_void_p]
         lib.gdn_fwd_sm100.restype = ctypes.c_int
+        lib.gdn_fwd_workspace_bytes.argtypes = [ctypes.POINTER(GdnFwdArgs)]
+        lib.gdn_fwd_workspace_bytes.restype = ctypes.c_uint64
         lib.gdn_wy_prep_sm100.argtypes = [ctypes.POINTER(GdnFwdArgs), ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_void_p]
         lib.gdn_wy_prep_sm100.restype = ctypes.c_int

@@ -14,6 +14,7 @@ missing, or the device is not a B200, the call raises instead of falling back.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -32,6 +33,21 @@ class GdnError(RuntimeError):
 
 _DTYPES = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
 _status_words: dict[int, torch.Tensor] = {}
+_workspaces: dict[int, torch.Tensor] = {}
+
+# Upper bound of the per-device scratch of the two-kernel path; longer inputs
+# run in several segments of chunks, so memory does not grow with T.
+WORKSPACE_CAP_BYTES = int(os.environ.get("GDN_B200_WORKSPACE_MB", "256")) << 20
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Cached uint8 scratch on ``device``; grows (never shrinks) on demand."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _workspaces.get(idx)
+    if w is None or w.numel() < nbytes:
+        w = torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _workspaces[idx] = w
+    return w
 
 
 def _status_word(device: torch.device) -> torch.Tensor:
@@ -111,7 +127,7 @@ def _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status) -> _lib
 
 
 def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output_dtype=None,
-                  output_final_state=True, block_v=0, check=False):
+                  output_final_state=True, block_v=0, check=False, fused=False):
     """Chunked Gated DeltaNet forward on a B200.
 
     Args:
@@ -125,6 +141,9 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
         output_final_state: return the final state (else None)
         block_v: V columns per CTA (0 = choose)
         check: synchronise and raise if the kernel reported an error
+        fused: run the single fused kernel instead of the two-kernel path
+            (chunk-parallel WY/UT preparation + state scan); both give the
+            same results, the fused one needs no scratch memory
     Returns:
         (o [B, T, H, V], h_final [B, H, V, K] fp32 or None)
 
@@ -151,6 +170,13 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
     ht = torch.empty(B, H, V, K, dtype=torch.float32, device=dev) if output_final_state else None
     status = _status_word(dev)
     args = _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status)
+    if not fused:
+        need = int(lib.gdn_fwd_workspace_bytes(ctypes.byref(args)))
+        per_head = B * H * (40960 + V * K * 4)
+        nbytes = max(min(need, WORKSPACE_CAP_BYTES), per_head)
+        ws = _workspace(dev, nbytes)
+        args.workspace = ws.data_ptr()
+        args.workspace_bytes = ws.numel()
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
         rc = lib.gdn_fwd_sm100(ctypes.byref(args), ctypes.c_void_p(stream))
