@@ -41,7 +41,8 @@ enum gdn_status {
   GDN_ERR_ALIGNMENT = 3,        /* base/stride not 16-byte aligned (TMA)     */
   GDN_ERR_CUDA = 4,             /* a CUDA runtime call failed                */
   GDN_ERR_TIMEOUT = 5,          /* a device-side bounded wait expired        */
-  GDN_ERR_NO_DEVICE = 6         /* no sm_100 device is current               */
+  GDN_ERR_NO_DEVICE = 6,        /* no sm_100 device is current               */
+  GDN_ERR_SCRATCH_LIMIT = 7     /* request too large for the fixed scratch   */
 };
 
 /*
@@ -108,6 +109,29 @@ int gdn_fwd_sm100(const gdn_fwd_args* args, void* stream);
  * segments.  Returns 0 for invalid arguments.
  */
 uint64_t gdn_fwd_workspace_bytes(const gdn_fwd_args* args);
+
+/*
+ * Allocation-free variant of gdn_fwd_sm100, for callers that must not
+ * allocate device memory when they call it: runtimes that plan all device
+ * memory at start-up and forbid later allocation, plug-ins whose host
+ * framework owns the memory pool, and code that cannot afford the device-wide
+ * synchronisation cudaMalloc may cause.  It runs the two-kernel path with its
+ * scratch in a fixed GDN_NOALLOC_SCRATCH_BYTES array inside the library
+ * (args->workspace is ignored) and makes no allocation itself.
+ * - Limit: B*H*(40960 + V*K*4) bytes must fit in the array (one chunk of
+ *   operands plus one fp32 state per (batch, head)); larger requests return
+ *   GDN_ERR_SCRATCH_LIMIT before any device work.  Longer sequences are run
+ *   in as many segments of chunks as the array requires.
+ * - The array is reserved on a device from the first call there (lazy
+ *   module loading) until the process exits; that first call also looks up
+ *   the array's device address, so make it before any stream capture.
+ * - All calls share the array: calls that may overlap on the GPU (other
+ *   streams, other host threads on the same device) race and must be
+ *   serialised by the caller.
+ * No counterpart in the reference, whose wrapper always allocates.
+ */
+#define GDN_NOALLOC_SCRATCH_BYTES (32ull << 20)
+int gdn_fwd_sm100_noalloc(const gdn_fwd_args* args, void* stream);
 
 /*
  * Chunk-parallel WY/UT preparation only (the per-chunk, state-independent

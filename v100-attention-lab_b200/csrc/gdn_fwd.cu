@@ -911,6 +911,7 @@ extern "C" const char* gdn_status_string(int code) {
     case GDN_ERR_CUDA: return "CUDA runtime error";
     case GDN_ERR_TIMEOUT: return "device-side wait timed out (kernel aborted)";
     case GDN_ERR_NO_DEVICE: return "current device is not sm_100 (B200)";
+    case GDN_ERR_SCRATCH_LIMIT: return "request too large for the fixed no-alloc scratch (B*H*(40960+V*K*4) bytes)";
   }
   return "unknown status";
 }

@@ -15,7 +15,7 @@ SRC_DIR = os.path.join(os.path.dirname(PKG_DIR), "csrc")
 INCLUDE_DIR = os.path.join(os.path.dirname(os.path.dirname(PKG_DIR)), "include")
 LIB_PATH = os.path.join(PKG_DIR, "libgdn_b200.so")
 
-SOURCES = ["gdn_fwd.cu", "gdn_wy_scan.cu"]
+SOURCES = ["gdn_fwd.cu", "gdn_wy_scan.cu", "gdn_noalloc.cu"]
 HEADERS = ["tc.cuh", "tmap.h", "gdn_common.cuh", "gdn_wy_scan.h"]
 
 NVCC_FLAGS = [

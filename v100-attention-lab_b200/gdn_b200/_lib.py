@@ -25,10 +25,11 @@ ERR_ALIGNMENT = 3
 ERR_CUDA = 4
 ERR_TIMEOUT = 5
 ERR_NO_DEVICE = 6
+ERR_SCRATCH_LIMIT = 7
 
 # Every symbol include/gdn_b200.h declares.
-EXPORTED_SYMBOLS = ("gdn_fwd_sm100", "gdn_fwd_workspace_bytes", "gdn_wy_prep_sm100", "gdn_selftest_wait_timeout",
-                    "gdn_status_string", "gdn_abi_version")
+EXPORTED_SYMBOLS = ("gdn_fwd_sm100", "gdn_fwd_sm100_noalloc", "gdn_fwd_workspace_bytes", "gdn_wy_prep_sm100",
+                    "gdn_selftest_wait_timeout", "gdn_status_string", "gdn_abi_version")
 
 _i64x3 = ctypes.c_int64 * 3
 
@@ -95,6 +96,8 @@ def load(build_if_missing: bool = False) -> ctypes.CDLL:
             raise RuntimeError(f"gdn_b200: {path} lacks symbols {missing}")
         lib.gdn_fwd_sm100.argtypes = [ctypes.POINTER(GdnFwdArgs), ctypes.c_void_p]
         lib.gdn_fwd_sm100.restype = ctypes.c_int
+        lib.gdn_fwd_sm100_noalloc.argtypes = [ctypes.POINTER(GdnFwdArgs), ctypes.c_void_p]
+        lib.gdn_fwd_sm100_noalloc.restype = ctypes.c_int
         lib.gdn_fwd_workspace_bytes.argtypes = [ctypes.POINTER(GdnFwdArgs)]
         lib.gdn_fwd_workspace_bytes.restype = ctypes.c_uint64
         lib.gdn_wy_prep_sm100.argtypes = [ctypes.POINTER(GdnFwdArgs), ctypes.c_void_p, ctypes.c_void_p,
