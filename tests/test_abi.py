@@ -107,8 +107,10 @@ def test_null_args_pointer(lib):
 
 def test_workspace_query(lib):
     a = _args(B=2, T=4096, H=16)
-    # one 40 KB packet per (b, h, chunk) plus one fp32 state per (b, h)
-    assert lib.gdn_fwd_workspace_bytes(ctypes.byref(a)) == 2 * 16 * (64 * 40960 + 128 * 128 * 4)
+    from gdn_b200 import _lib
+    pk = _lib.PACKET_BYTES_PER_CHUNK
+    # one packet per (b, h, chunk) plus one fp32 state per (b, h)
+    assert lib.gdn_fwd_workspace_bytes(ctypes.byref(a)) == 2 * 16 * (64 * pk + 128 * 128 * 4)
     a = _args(T=100)
-    assert lib.gdn_fwd_workspace_bytes(ctypes.byref(a)) == 1 * 1 * (2 * 40960 + 128 * 128 * 4)
+    assert lib.gdn_fwd_workspace_bytes(ctypes.byref(a)) == 1 * 1 * (2 * pk + 128 * 128 * 4)
     assert lib.gdn_fwd_workspace_bytes(None) == 0

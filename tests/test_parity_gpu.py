@@ -60,23 +60,29 @@ def test_wy_prep_stage(gdn):
         assert ora.max_rel(f(U[:, :, c]), st["U"]) < 1e-4   # U uses the hi+lo split
 
 
-def test_two_kernel_matches_fused(gdn):
-    """The two paths compute the same operands; results agree to fp32 rounding."""
+def test_two_kernel_and_fused_paths_both_match_oracle(gdn):
+    """The two-kernel path (state update regrouped as e^{b_C} S + N S + c) and
+    the fused single-kernel path round differently; each meets the tolerance
+    against the oracle on the same inputs, and they agree with each other to
+    within twice that."""
     qd, kd, vd, bd, gd, h0 = make(2, 700, 3, seed=41, dtype=torch.bfloat16, h0_std=0.1)
     o1, h1 = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
     o2, h2 = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True,
                                fused=True)
-    assert rel(o1, o2.float().cpu().numpy()) < 1e-5
-    assert rel(h1, h2.float().cpu().numpy()) < 1e-5
+    o_ref, h_ref = oracle(qd, kd, vd, bd, gd, h0)
+    for o, h in ((o1, h1), (o2, h2)):
+        assert rel(o, o_ref) < TOL
+        assert rel(h, h_ref) < TOL
+    assert rel(o1, o2.float().cpu().numpy()) < 2 * TOL
 
 
 @pytest.mark.parametrize("cap_chunks", [1, 3])
 def test_segmented_workspace(gdn, cap_chunks, monkeypatch):
     """A workspace smaller than the sequence: several prep/scan segments with
     the state carried between them."""
-    from gdn_b200 import ops
+    from gdn_b200 import _lib, ops
     B, H = 1, 2
-    cap = B * H * (cap_chunks * 40960 + 128 * 128 * 4)
+    cap = B * H * (cap_chunks * _lib.PACKET_BYTES_PER_CHUNK + 128 * 128 * 4)
     monkeypatch.setattr(ops, "WORKSPACE_CAP_BYTES", cap)
     monkeypatch.setattr(ops, "_workspaces", {})
     qd, kd, vd, bd, gd, h0 = make(B, 450, H, seed=42, dtype=torch.float16, h0_std=0.1)

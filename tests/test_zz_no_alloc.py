@@ -43,8 +43,8 @@ def _noalloc(env, q, k, v, beta, g, h0):
 def test_noalloc_matches_regular_entry_point_twice(env):
     from gpu_util import TOL, make, rel
     gdn, _lib, ops, _ = env
-    # B*H = 32 heads and 32 chunks need ~42 MB of scratch in one piece, so
-    # the 32 MiB array is used in two segments with the state carried over
+    # B*H = 32 heads and 32 chunks need ~103 MB of scratch in one piece, so
+    # the 32 MiB array is used in four segments with the state carried over
     for call, seed in enumerate((51, 52)):
         qd, kd, vd, bd, gd, h0 = make(2, 2048, 16, seed=seed, dtype=torch.bfloat16, h0_std=0.1)
         rc, o, ht = _noalloc(env, qd, kd, vd, bd, gd, h0)
@@ -58,7 +58,7 @@ def test_noalloc_matches_regular_entry_point_twice(env):
 
 def test_noalloc_refuses_requests_beyond_its_scratch(env):
     _, _lib, _, _ = env
-    # 64 x 32 (batch, head) pairs need ~213 MB for one chunk each
+    # 64 x 32 (batch, head) pairs need ~336 MB for one chunk each
     q = torch.zeros(64, 1, 32, 128, dtype=torch.bfloat16, device="cuda")
     beta = torch.zeros(64, 1, 32, device="cuda")
     rc, _, _ = _noalloc(env, q, q.clone(), q.clone(), beta, beta.clone(), None)

@@ -757,6 +757,7 @@ int launch_out(const gdn_fwd_args* a, const FwdParams& p, int grid, cudaStream_t
 
 #ifdef GDN_TRACE
 long long* g_trace = nullptr;
+long long* g_trace_wy = nullptr;
 #endif
 
 // Two-kernel path: per segment of chunks, the WY/UT prep kernel writes one
@@ -776,21 +777,19 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
   memset(&sp, 0, sizeof(sp));
   if (!make_input_map(&wp.tm_q, a, a->q, a->q_stride, kK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_input_map(&wp.tm_k, a, a->k, a->k_stride, kK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_input_map(&sp.tm_v, a, a->v, a->v_stride, kV, BV, CU_TENSOR_MAP_SWIZZLE_64B))
+      !make_input_map(&wp.tm_v, a, a->v, a->v_stride, kV, 64, CU_TENSOR_MAP_SWIZZLE_128B))
     return GDN_ERR_CUDA;
-  sp.tm_q = wp.tm_q;
-  sp.tm_k = wp.tm_k;
-  wp.beta = sp.beta = a->beta;
-  wp.g = sp.g = a->g;
+  wp.beta = a->beta;
+  wp.g = a->g;
   wp.status = sp.status = a->status;
   wp.packets = packets;
   sp.packets = packets;
-  wp.sb_b = sp.sb_b = a->beta_stride[0];
-  wp.sb_t = sp.sb_t = a->beta_stride[1];
-  wp.sb_h = sp.sb_h = a->beta_stride[2];
-  wp.sg_b = sp.sg_b = a->g_stride[0];
-  wp.sg_t = sp.sg_t = a->g_stride[1];
-  wp.sg_h = sp.sg_h = a->g_stride[2];
+  wp.sb_b = a->beta_stride[0];
+  wp.sb_t = a->beta_stride[1];
+  wp.sb_h = a->beta_stride[2];
+  wp.sg_b = a->g_stride[0];
+  wp.sg_t = a->g_stride[1];
+  wp.sg_h = a->g_stride[2];
   sp.so_b = a->o_stride[0];
   sp.so_t = a->o_stride[1];
   sp.so_h = a->o_stride[2];
@@ -800,6 +799,10 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
   wp.T = sp.T = a->T;
   wp.H = sp.H = a->H;
   sp.nslice = kV / BV;
+#ifdef GDN_TRACE
+  sp.trace = g_trace;
+  wp.trace = g_trace_wy;
+#endif
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int in_bf16 = a->in_dtype == GDN_DTYPE_BF16;
   for (int c0 = 0; c0 < NT; c0 += ns_max) {
@@ -809,7 +812,7 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
     sp.h0 = (c0 == 0) ? a->h0 : state;
     int rc = run_wy(in_bf16, wp, a->B * a->H * ns, s);
     if (rc != GDN_OK) return rc;
-    rc = run_scan(in_bf16, a->out_dtype, sp, a->B * a->H * sp.nslice, s);
+    rc = run_scan(a->out_dtype, sp, a->B * a->H * sp.nslice, s);
     if (rc != GDN_OK) return rc;
   }
   return GDN_OK;
@@ -911,7 +914,7 @@ extern "C" const char* gdn_status_string(int code) {
     case GDN_ERR_CUDA: return "CUDA runtime error";
     case GDN_ERR_TIMEOUT: return "device-side wait timed out (kernel aborted)";
     case GDN_ERR_NO_DEVICE: return "current device is not sm_100 (B200)";
-    case GDN_ERR_SCRATCH_LIMIT: return "request too large for the fixed no-alloc scratch (B*H*(40960+V*K*4) bytes)";
+    case GDN_ERR_SCRATCH_LIMIT: return "request too large for the fixed no-alloc scratch (B*H*(98560+V*K*4) bytes)";
   }
   return "unknown status";
 }
@@ -927,4 +930,5 @@ extern "C" uint64_t gdn_fwd_workspace_bytes(const gdn_fwd_args* a) {
 #ifdef GDN_TRACE
 // Trace builds only: device buffer of NT * 16 int64 timestamps for CTA 0.
 extern "C" void gdn_set_trace_buffer(long long* buf) { gdn::g_trace = buf; }
+extern "C" void gdn_set_trace_buffer_wy(long long* buf) { gdn::g_trace_wy = buf; }
 #endif

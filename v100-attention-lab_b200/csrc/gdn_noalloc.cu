@@ -23,6 +23,7 @@
 // GPU (different streams, or different host threads on one device) race on
 // the array: serialise them.
 #include "../../include/gdn_b200.h"
+#include "gdn_wy_scan.h"
 
 #include <cuda_runtime.h>
 
@@ -66,7 +67,7 @@ extern "C" int gdn_fwd_sm100_noalloc(const gdn_fwd_args* args, void* stream) {
   // One chunk per (batch, head) must fit, next to one fp32 state per (b, h):
   // the sequence is then processed in as many segments as the array needs.
   const uint64_t pairs = uint64_t(args->B) * uint64_t(args->H);
-  const uint64_t per_pair = 40960ull + uint64_t(args->K) * uint64_t(args->V) * 4ull;
+  const uint64_t per_pair = gdn::kPacketBytesPerChunk + uint64_t(args->K) * uint64_t(args->V) * 4ull;
   if (pairs > gdn::kScratchBytes / per_pair) return GDN_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   const int rc = gdn::scratch_for_current_device(&scratch);

@@ -1,22 +1,33 @@
-// Two-kernel chunked GDN forward for B200 (sm_100a):
+// Two-kernel chunked GDN forward for B200 (sm_100a).
 //
-//   gdn_wy_kernel   chunk-parallel WY/UT preparation, one CTA per (b, h, chunk),
-//                   two CTAs per SM.  Everything state-independent and
-//                   V-independent is done once per chunk here:
-//                     S = [K;Q]K^T, A and P (gdn_ref.py:76-80, :87-88),
-//                     T = (I+A)^-1 in fp32, W = T diag(beta e^b) K (gdn_ref.py:85),
-//                   and written to a 40 KB "packet" in the exact shared-memory
-//                   image the scan kernel feeds to its tensor cores:
-//                     [W fp16 (2 x 8 KB) | Tb_hi | P fp16 | Tb_lo]  (8 KB each)
-//                   with Tb = T diag(beta) split hi + lo in the input dtype.
+// Per chunk of C = 64 steps (b = in-chunk cumsum of g, gdn_ref.py:76-99), the
+// state update and the output are affine in the chunk-start state S = h^T
+// (K x V):
+//
+//   S' = e^{b_C} S + N S + c            N = -Kbar^T W          (K x K)
+//                                      c =  Kbar^T U          (K x V)
+//   o  = Q' S + o_intra                 Q' = Qhat - P W        (C x K)
+//                                      o_intra = P U          (C x V)
+//
+// with Kbar = e^{b_C - b} k, Qhat = e^{b} q, P = tril(Q K^T * e^{b_t - b_j}),
+// W = T diag(beta e^b) K, U = T diag(beta) V, T = (I + A)^-1.  This is the
+// reference's own two-GEMM state update h0 (e^{b_C} I - Wbar^T K) + Ubar^T K
+// (gdn_ref.py:92-98) and its output u-form (gdn_ref.py:86-90) regrouped so
+// that everything except one K x K by K x V product per chunk is independent
+// of the state.
+//
+//   gdn_wy_kernel   chunk-parallel, one CTA per (b, h, chunk), two per SM:
+//                   S = [K;Q]K^T -> A, P; T in fp32; W, U (U split hi + lo);
+//                   then N, c, Q', o_intra on the tensor cores, written as a
+//                   96 KB packet of fp16 images in the exact shared-memory
+//                   layout the scan feeds to its tensor cores.
 //   gdn_scan_kernel one CTA per (b, h, 32-wide V slice), serial over chunks:
-//                   U = Tb V (gdn_ref.py:84), u = U - W h^T, h = e^{b_C} h +
-//                   Kbar^T u, o = Qhat h^T + P u; q and k are scaled and
-//                   converted to fp16 in place in the stage buffers.
+//                   one 128x128x32 product per chunk on the critical path
+//                   (N S), plus Q' S off it; the state stays in registers.
 //
-// The packets are scratch memory of 40 KB per (b, h, chunk); long sequences
-// are processed in segments of chunks so the scratch stays bounded, the
-// state being carried between segments (gdn_ref.py semantics are unchanged).
+// The packets are scratch memory (kPacketBytesPerChunk per (b, h, chunk));
+// long sequences are processed in segments of chunks so the scratch stays
+// bounded, the state being carried between segments.
 #include "gdn_common.cuh"
 #include "tmap.h"
 #include "gdn_wy_scan.h"
@@ -26,25 +37,62 @@
 
 namespace gdn {
 
-constexpr uint32_t kPacketBytes = 40960;
-// packet offsets
-constexpr uint32_t kPkW0 = 0, kPkW1 = 8192, kPkTbHi = 16384, kPkP = 24576, kPkTbLo = 32768;
+constexpr uint32_t kPacketBytes = uint32_t(kPacketBytesPerChunk);
+// packet layout (bytes)
+namespace pkt {
+constexpr uint32_t kN = 0;        // N fp16, 128 x 128, K-major SW128: 2 column blocks of 16 KB
+constexpr uint32_t kQ = 32768;    // Q' fp16, 64 x 128, K-major SW128: 2 column blocks of 8 KB
+constexpr uint32_t kHdr = 49152;  // fp32 e^{b_C}
+constexpr uint32_t kHead = 49408; // [N | Q' | hdr]: one bulk copy
+constexpr uint32_t kCs = 49408;   // c fp16, 4 V slices x (128 rows x 64 B, SW64 rows)
+constexpr uint32_t kOs = 82176;   // o_intra fp16, 4 V slices x (64 rows x 64 B, SW64 rows)
+static_assert(kOs + 4 * 4096 == kPacketBytesPerChunk, "packet size");
+}  // namespace pkt
 
-// =========================================================== WY/UT prep kernel
+// =========================================================== prep kernel
 namespace wy {
-constexpr int kThreads = 160;  // warps 0-3: prep (TMEM lanes 0-127), warp 4: TMA + MMA
-constexpr uint32_t kq = 0;          // [k;q] stacked: 2 col-blocks x (64 k rows | 64 q rows) x 128 B
-constexpr uint32_t tw = 32768;      // Tw (input dtype), 64 rows x 128 B
-constexpr uint32_t pk = 40960;      // packet image, 40 KB
-constexpr uint32_t amat = 81920;    // fp32 A / T, 64 x kAStride
-constexpr uint32_t vec = amat + kC * kAStride * 4;
+constexpr int kThreads = 160;      // warps 0-3: prep (TMEM lanes 0-127), warp 4: TMA + MMA
+constexpr uint32_t kq = 0;         // [k0 | q0 | k1 | q1] 8 KB each (k later -> Kbar fp16 in place)
+constexpr uint32_t vt = 32768;     // [v0 | v1] 8 KB each, later U_hi fp16
+constexpr uint32_t amat = 49152;   // fp32 A / T (64 x kAStride), later W fp16 [w0 | w1]
+constexpr uint32_t tw = 66560;     // Tw (input dtype), 64 x 128 B
+constexpr uint32_t tb = 74752;     // Tb_hi | Tb_lo (input dtype), later U_lo fp16
+constexpr uint32_t p16 = 91136;    // P fp16, 64 x 128 B
+constexpr uint32_t vec = 99328;    // kVecN x 64 fp32
 constexpr uint32_t bars = vec + kVecN * kC * 4;
-constexpr uint32_t misc = bars + 8 * 8;
+constexpr uint32_t misc = bars + 16 * 8;
 constexpr uint32_t total = misc + 32;
 constexpr uint32_t alloc = total + 1024;
-constexpr uint32_t kTmS = 0, kTmW = 64;  // TMEM columns (W is M=64: 128 columns)
-enum { B_FULL = 0, B_SFULL, B_TREADY, B_WFULL, B_DONE, B_COUNT };
+static_assert(amat + kC * kAStride * 4 <= tw, "A/T overlaps Tw");
+// TMEM columns: S 0-63 (M=128); W 0-127, U 128-255 (M=64); PW 0-127, PU 128-255 (M=64);
+// N 0-127, c 128-255 (M=128).  Packet pieces are staged in shared memory that the
+// finished MMAs no longer read and leave in bulk copies:
+//   Q' in place over q; o_intra over P (slices 0-1) and Tw (slices 2-3);
+//   N over U_hi (block 0) and U_lo (block 1); c over Kbar (slices 0-1) and W (slices 2-3).
+enum { B_FULL = 0, B_SFULL, B_TREADY, B_WUFULL, B_EPA, B_PFULL, B_EPC, B_NCFULL, B_DONE, B_COUNT };
 }  // namespace wy
+
+__device__ __forceinline__ uint4 pack8_f16(const float* x) {
+  uint4 w;
+  w.x = Cvt<__half>::pack(x[0], x[1]);
+  w.y = Cvt<__half>::pack(x[2], x[3]);
+  w.z = Cvt<__half>::pack(x[4], x[5]);
+  w.w = Cvt<__half>::pack(x[6], x[7]);
+  return w;
+}
+
+// GDN_TRACE builds: clock64 at phase boundaries of CTAs 0-63 (24 slots each),
+// plus globaltimer at start / end and the SM id.
+#ifdef GDN_TRACE
+#define WY_TR(slot)                                                                  \
+  do {                                                                               \
+    if (P.trace != nullptr && blockIdx.x < 64) P.trace[blockIdx.x * 24 + (slot)] = clock64(); \
+  } while (0)
+#else
+#define WY_TR(slot) \
+  do {              \
+  } while (0)
+#endif
 
 template <typename InT>
 __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_constant__ WyParams P) {
@@ -61,9 +109,11 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
   const int hh = bh % P.H, bb = bh / P.H;
   const int chunk = P.c0 + il;
   const int t0 = chunk * kC;
+  uint8_t* const pkg = P.packets + (size_t(bh) * P.NS + il) * kPacketBytes;
 
   if (tid == 0) {
-    for (int i = 0; i < wy::B_COUNT; ++i) mbar_init(&bars[i], i == wy::B_TREADY ? 4 : 1);
+    for (int i = 0; i < wy::B_COUNT; ++i)
+      mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC) ? 4 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -75,14 +125,27 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
   tc_fence_after();
   const uint32_t tmem = *tmem_base_p;
   const uint32_t sb = smem_u32(sm);
+#ifdef GDN_TRACE
+  if (tid == 0 && P.trace != nullptr && blockIdx.x < 64) {
+    long long gt;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    P.trace[blockIdx.x * 24 + 20] = gt;
+    P.trace[blockIdx.x * 24 + 22] = smid;
+  }
+#endif
+  if (tid == 0) WY_TR(0);
 
   if (warp == 4) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(&bars[wy::B_FULL], 32768);
+      mbar_arrive_expect_tx(&bars[wy::B_FULL], 49152);
       tma_load_4d(sm + wy::kq, &P.tm_k, &bars[wy::B_FULL], 0, t0, hh, bb);
       tma_load_4d(sm + wy::kq + 8192, &P.tm_q, &bars[wy::B_FULL], 0, t0, hh, bb);
       tma_load_4d(sm + wy::kq + 16384, &P.tm_k, &bars[wy::B_FULL], 64, t0, hh, bb);
       tma_load_4d(sm + wy::kq + 24576, &P.tm_q, &bars[wy::B_FULL], 64, t0, hh, bb);
+      tma_load_4d(sm + wy::vt, &P.tm_v, &bars[wy::B_FULL], 0, t0, hh, bb);
+      tma_load_4d(sm + wy::vt + 8192, &P.tm_v, &bars[wy::B_FULL], 64, t0, hh, bb);
     }
     // in-chunk cumsum of g (log2 units) and beta; zero past T (gdn_ref.py:102-114)
     constexpr float kLog2e = 1.4426950408889634f;
@@ -101,54 +164,97 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       }
     }
     xb += __shfl_sync(0xffffffffu, xa, 31);
+    const float bC = __shfl_sync(0xffffffffu, xb, 31);
     vec[V_B2 * kC + lane] = xa;
     vec[V_B2 * kC + lane + 32] = xb;
     vec[V_BETA * kC + lane] = (ta < P.T) ? bp[(long long)ta * P.sb_t] : 0.f;
     vec[V_BETA * kC + lane + 32] = (tb < P.T) ? bp[(long long)tb * P.sb_t] : 0.f;
     vec[V_EB * kC + lane] = fast_exp2(xa);
     vec[V_EB * kC + lane + 32] = fast_exp2(xb);
+    vec[V_DD * kC + lane] = fast_exp2(bC - xa);
+    vec[V_DD * kC + lane + 32] = fast_exp2(bC - xb);
   }
   __syncthreads();  // vec visible
 
   constexpr uint32_t kInBf16 = Cvt<InT>::kIsBf16;
   bool ok = true;
   if (warp == 4) {
-    if (lane == 0) {
-      ok = mbar_wait(&bars[wy::B_FULL], 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        const uint32_t id_s = idesc_f16(128, 64, kInBf16, 0, 0);
+    // ------------------------------------------------ MMA issue (the whole warp; elect.sync inside)
+    ok = mbar_wait_warp(&bars[wy::B_FULL], 0, abort_flag);
+    if (lane == 0) WY_TR(1);
+    if (ok) {
+      // S = [K;Q] K^T: M=128 (k rows then q rows), N=64, K=128
+      tc_fence_after();
+      const uint32_t id_s = idesc_f16(128, 64, kInBf16, 0, 0);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t a = sb + wy::kq + (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_f16_ss(tmem + wy::kTmS, sdesc(a, 16, 1024, kSw128), sdesc(a, 16, 1024, kSw128), id_s, kk > 0);
-        }
-        mma_commit(&bars[wy::B_SFULL]);
-        ok = mbar_wait(&bars[wy::B_TREADY], 0, abort_flag);
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t a = sb + wy::kq + (kk >> 2) * 16384 + (kk & 3) * 32;
+        mma_f16_ss_warp(tmem, sdesc(a, 16, 1024, kSw128), sdesc(a, 16, 1024, kSw128), id_s, kk > 0);
       }
-      if (ok) {
-        tc_fence_after();
-        // W = Tw K: M=64 (Tw rows), N=128 (d), K=64 (j); B = k tile read MN-major
-        const uint32_t id_w = idesc_f16(64, 128, kInBf16, 0, 1);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_f16_ss(tmem + wy::kTmW, sdesc(sb + wy::tw + kk * 32, 16, 1024, kSw128),
-                     sdesc(sb + wy::kq + kk * 2048, 16384, 1024, kSw128), id_w, kk > 0);
-        mma_commit(&bars[wy::B_WFULL]);
-      }
-      if (!ok) *abort_flag = 1;
+      mma_commit_warp(&bars[wy::B_SFULL]);
+      ok = mbar_wait_warp(&bars[wy::B_TREADY], 0, abort_flag);
     }
+    if (ok) {
+      // W = Tw K (M=64, N=128, K=64; B = k read MN-major) -> cols 0-127
+      // U = Tb_hi V + Tb_lo V (M=64, N=128, K=64 twice)   -> cols 128-255
+      tc_fence_after();
+      const uint32_t id_w = idesc_f16(64, 128, kInBf16, 0, 1);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_ss_warp(tmem, sdesc(sb + wy::tw + kk * 32, 16, 1024, kSw128),
+                        sdesc(sb + wy::kq + kk * 2048, 16384, 1024, kSw128), id_w, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::tb + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024, kSw128),
+                        sdesc(sb + wy::vt + (kk & 3) * 2048, 8192, 1024, kSw128), id_w, kk > 0);
+      mma_commit_warp(&bars[wy::B_WUFULL]);
+      ok = mbar_wait_warp(&bars[wy::B_EPA], 0, abort_flag);
+    }
+    if (ok) {
+      // P W -> cols 0-127, P (U_hi + U_lo) -> cols 128-255  (M=64, N=128, K=64; B MN-major)
+      tc_fence_after();
+      const uint32_t id_p = idesc_f16(64, 128, 0, 0, 1);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_ss_warp(tmem, sdesc(sb + wy::p16 + kk * 32, 16, 1024, kSw128),
+                        sdesc(sb + wy::amat + kk * 2048, 8192, 1024, kSw128), id_p, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::p16 + (kk & 3) * 32, 16, 1024, kSw128),
+                        sdesc(sb + (kk < 4 ? wy::vt : wy::tb) + (kk & 3) * 2048, 8192, 1024, kSw128), id_p,
+                        kk > 0);
+      mma_commit_warp(&bars[wy::B_PFULL]);
+      ok = mbar_wait_warp(&bars[wy::B_EPC], 0, abort_flag);
+    }
+    if (ok) {
+      // Kbar^T W -> cols 0-127, Kbar^T (U_hi + U_lo) -> cols 128-255  (M=128, N=128, K=64; A and B MN-major)
+      tc_fence_after();
+      const uint32_t id_n = idesc_f16(128, 128, 0, 1, 1);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_ss_warp(tmem, sdesc(sb + wy::kq + kk * 2048, 16384, 1024, kSw128),
+                        sdesc(sb + wy::amat + kk * 2048, 8192, 1024, kSw128), id_n, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::kq + (kk & 3) * 2048, 16384, 1024, kSw128),
+                        sdesc(sb + (kk < 4 ? wy::vt : wy::tb) + (kk & 3) * 2048, 8192, 1024, kSw128), id_n,
+                        kk > 0);
+      mma_commit_warp(&bars[wy::B_NCFULL]);
+    }
+    if (!ok && lane == 0) *abort_flag = 1;
     __syncwarp();
   } else {
-    // ---------------------------------------------------------------- prep (warps 0-3)
-    const int ptid = tid;  // 0..127 = TMEM lane
+    // ------------------------------------------------ prep (warps 0-3, thread = TMEM lane)
+    const int ptid = tid;
     const float b2first = vec[V_B2 * kC], b2last = vec[V_B2 * kC + kC - 1];
     const float ref = 0.5f * (b2first + b2last);
     const bool prod_form = (b2first - b2last) < 200.f;
     if (ptid < 64) amat[ptid * kAStride + 64] = fast_exp2(ref - vec[V_B2 * kC + ptid]);
     named_bar(2, 128);
     ok = mbar_wait_warp(&bars[wy::B_SFULL], 0, abort_flag);
-    if (!bar_any(1, 128, !ok || *abort_flag)) {
+    if (ptid == 0) WY_TR(2);
+    if (bar_any(1, 128, !ok || *abort_flag)) ok = false;
+    if (ok) {
       tc_fence_after();
       // rows 0-63: A[t][m] = beta_t exp(b_t - b_m) (k_t.k_m), m < t   (TMEM lanes 0-63 = K K^T)
       // rows 64-127: P[t][m] = exp(b_t - b_m) (q_t.k_m), m <= t      (lanes 64-127 = Q K^T)
@@ -157,11 +263,11 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       const float et = fast_exp2(b2t - ref);
       const float bt = (ptid < 64) ? vec[V_BETA * kC + t] : 1.f;
       float* arow = amat + t * kAStride;
-      uint8_t* pimg = sm + wy::pk + kPkP;
+      uint8_t* pimg = sm + wy::p16;
 #pragma unroll 1
       for (int cg = 0; cg < 4; ++cg) {
         float s[16];
-        tmem_ld16w(tmem_addr(tmem + wy::kTmS, warp * 32, cg * 16), s);
+        tmem_ld16w(tmem_addr(tmem, warp * 32, cg * 16), s);
         float x[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
@@ -175,27 +281,22 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
           for (int e = 0; e < 16; e += 4)
             *reinterpret_cast<float4*>(arow + cg * 16 + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
         } else {
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            uint4 w;
-            w.x = Cvt<__half>::pack(x[8 * h2 + 0], x[8 * h2 + 1]);
-            w.y = Cvt<__half>::pack(x[8 * h2 + 2], x[8 * h2 + 3]);
-            w.z = Cvt<__half>::pack(x[8 * h2 + 4], x[8 * h2 + 5]);
-            w.w = Cvt<__half>::pack(x[8 * h2 + 6], x[8 * h2 + 7]);
-            *reinterpret_cast<uint4*>(pimg + sw128_off(t, 2 * cg + h2)) = w;
-          }
+          *reinterpret_cast<uint4*>(pimg + sw128_off(t, 2 * cg)) = pack8_f16(x);
+          *reinterpret_cast<uint4*>(pimg + sw128_off(t, 2 * cg + 1)) = pack8_f16(x + 8);
         }
       }
       tc_fence_before();
       named_bar(1, 128);
+      if (ptid == 0) WY_TR(3);
       invert_unit_lower64(amat, ptid);  // T = (I + A)^-1 in place
-      // Tw = T diag(beta e^b) -> tw (MMA operand); Tb = T diag(beta) -> packet hi + lo
+      if (ptid == 0) WY_TR(4);
+      // Tw = T diag(beta e^b) -> tw; Tb = T diag(beta) -> hi + lo (input dtype, MMA operands)
       {
         const int r = ptid >> 1, half = ptid & 1;
         const float* trow = amat + r * kAStride;
         uint8_t* twp = sm + wy::tw;
-        uint8_t* hip = sm + wy::pk + kPkTbHi;
-        uint8_t* lop = sm + wy::pk + kPkTbLo;
+        uint8_t* hip = sm + wy::tb;
+        uint8_t* lop = sm + wy::tb + 8192;
 #pragma unroll 1
         for (int c = 4 * half; c < 4 * half + 4; ++c) {
           uint32_t ww[4], hi[4], lo[4];
@@ -216,101 +317,243 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[wy::B_TREADY]);
-      // W (M=64 layout: row 16w + l in TMEM lane 32w + l, l < 16) -> fp16 packet image
-      ok = mbar_wait_warp(&bars[wy::B_WFULL], 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        const int r = 16 * warp + (lane & 15);
+      if (ptid == 0) WY_TR(5);
+    }
+    // ---- epilogue A: W -> fp16 [t][k] (over A/T), U -> fp16 hi (over v) + lo (over Tb),
+    //      k -> Kbar = e^{b_C - b_t} k fp16 in place.  W and U are M=64 accumulators:
+    //      row 16w + l lives in TMEM lane 32w + l (l < 16).
+    ok = ok && mbar_wait_warp(&bars[wy::B_WUFULL], 0, abort_flag);
+    if (ptid == 0) WY_TR(6);
+    if (ok) {
+      tc_fence_after();
+      const int t = 16 * warp + (lane & 15);
 #pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 32) {
-          float w[32];
-          tmem_ld32w(tmem_addr(tmem + wy::kTmW, warp * 32, c0), w);
-          if (lane < 16) {
-            uint8_t* wimg = sm + wy::pk + (c0 >= 64 ? kPkW1 : kPkW0);
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        float w[32];
+        tmem_ld32w(tmem_addr(tmem, warp * 32, c0), w);
+        if (lane < 16) {
+          uint8_t* dst = sm + wy::amat + (c0 >> 6) * 8192;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              uint4 y;
-              y.x = Cvt<__half>::pack(w[8 * c + 0], w[8 * c + 1]);
-              y.y = Cvt<__half>::pack(w[8 * c + 2], w[8 * c + 3]);
-              y.z = Cvt<__half>::pack(w[8 * c + 4], w[8 * c + 5]);
-              y.w = Cvt<__half>::pack(w[8 * c + 6], w[8 * c + 7]);
-              *reinterpret_cast<uint4*>(wimg + sw128_off(r, ((c0 & 63) >> 3) + c)) = y;
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(dst + sw128_off(t, ((c0 & 63) >> 3) + c)) = pack8_f16(w + 8 * c);
+        }
+      }
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        float u[32];
+        tmem_ld32w(tmem_addr(tmem, warp * 32, 128 + c0), u);
+        if (lane < 16) {
+          uint8_t* dhi = sm + wy::vt + (c0 >> 6) * 8192;
+          uint8_t* dlo = sm + wy::tb + (c0 >> 6) * 8192;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float hi[8], lo[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              hi[e] = __half2float(__float2half_rn(u[8 * c + e]));
+              lo[e] = u[8 * c + e] - hi[e];
             }
+            const uint32_t off = sw128_off(t, ((c0 & 63) >> 3) + c);
+            *reinterpret_cast<uint4*>(dhi + off) = pack8_f16(hi);
+            *reinterpret_cast<uint4*>(dlo + off) = pack8_f16(lo);
           }
         }
-        tc_fence_before();
-        fence_async_smem();
       }
-    } else {
-      ok = false;
+      if (lane >= 16) {
+        const float dd = vec[V_DD * kC + t];
+#pragma unroll 1
+        for (int cb = 0; cb < 2; ++cb) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4* p = reinterpret_cast<uint4*>(sm + wy::kq + cb * 16384 + sw128_off(t, c));
+            const uint4 x = *p;
+            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+            uint32_t ys[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = Cvt<InT>::unpack(xs[e]);
+              ys[e] = Cvt<__half>::pack(f.x * dd, f.y * dd);
+            }
+            *p = make_uint4(ys[0], ys[1], ys[2], ys[3]);
+          }
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[wy::B_EPA]);
+      if (ptid == 0) WY_TR(7);
     }
+    // ---- epilogue C: Q' = e^{b_t} q_t - (P W)_t (in place over q) and o_intra = P U (M=64 rows)
+    ok = ok && mbar_wait_warp(&bars[wy::B_PFULL], 0, abort_flag);
+    if (ptid == 0) WY_TR(10);
+    if (bar_any(1, 128, !ok || *abort_flag)) ok = false;  // uniform: named barriers follow
+    if (ok) {
+      tc_fence_after();
+      const int t = 16 * warp + (lane & 15);
+      const float eb = vec[V_EB * kC + t];
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        float pw[32];
+        tmem_ld32w(tmem_addr(tmem, warp * 32, c0), pw);
+        if (lane < 16) {
+          uint8_t* qrow = sm + wy::kq + 8192 + (c0 >> 6) * 16384;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4* p = reinterpret_cast<uint4*>(qrow + sw128_off(t, ((c0 & 63) >> 3) + c));
+            const uint4 x = *p;
+            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = Cvt<InT>::unpack(xs[e]);
+              y[2 * e] = fmaf(eb, f.x, -pw[8 * c + 2 * e]);
+              y[2 * e + 1] = fmaf(eb, f.y, -pw[8 * c + 2 * e + 1]);
+            }
+            *p = pack8_f16(y);
+          }
+        }
+      }
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        float ou[32];
+        tmem_ld32w(tmem_addr(tmem, warp * 32, 128 + c0), ou);
+        if (lane < 16) {
+          const int sl = c0 >> 5;
+          uint8_t* dst = sm + (sl < 2 ? wy::p16 : wy::tw) + (sl & 1) * 4096;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + sw64_off(t, c)) = pack8_f16(ou + 8 * c);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[wy::B_EPC]);
+      fence_async_smem();
+      named_bar(1, 128);
+      if (ptid == 0) {
+        bulk_store(pkg + pkt::kQ, sm + wy::kq + 8192, 8192);
+        bulk_store(pkg + pkt::kQ + 8192, sm + wy::kq + 24576, 8192);
+        bulk_store(pkg + pkt::kOs, sm + wy::p16, 8192);
+        bulk_store(pkg + pkt::kOs + 8192, sm + wy::tw, 8192);
+        bulk_commit();
+        WY_TR(11);
+      }
+    }
+    // ---- epilogue B: N = -(Kbar^T W) and c = Kbar^T U (row k1 = TMEM lane)
+    ok = ok && mbar_wait_warp(&bars[wy::B_NCFULL], 0, abort_flag);
+    if (ptid == 0) WY_TR(8);
+    if (bar_any(1, 128, !ok || *abort_flag)) ok = false;
+    if (ok) {
+      tc_fence_after();
+      const int r = ptid;
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        float n[32];
+        tmem_ld32w(tmem_addr(tmem, warp * 32, c0), n);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) n[e] = -n[e];
+        uint8_t* dst = sm + (c0 < 64 ? wy::vt : wy::tb);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(dst + sw128_off(r, ((c0 & 63) >> 3) + c)) = pack8_f16(n + 8 * c);
+      }
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        float cv[32];
+        tmem_ld32w(tmem_addr(tmem, warp * 32, 128 + c0), cv);
+        const int sl = c0 >> 5;
+        uint8_t* dst = sm + (sl < 2 ? wy::kq + sl * 16384 : wy::amat + (sl & 1) * 8192);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + sw64_off(r, c)) = pack8_f16(cv + 8 * c);
+      }
+      if (r == 0) *reinterpret_cast<float*>(pkg + pkt::kHdr) = vec[V_EB * kC + kC - 1];
+      tc_fence_before();
+      fence_async_smem();
+      named_bar(1, 128);
+      if (ptid == 0) {
+        bulk_store(pkg + pkt::kN, sm + wy::vt, 16384);
+        bulk_store(pkg + pkt::kN + 16384, sm + wy::tb, 16384);
+        bulk_store(pkg + pkt::kCs, sm + wy::kq, 8192);
+        bulk_store(pkg + pkt::kCs + 8192, sm + wy::kq + 16384, 8192);
+        bulk_store(pkg + pkt::kCs + 16384, sm + wy::amat, 8192);
+        bulk_store(pkg + pkt::kCs + 24576, sm + wy::amat + 8192, 8192);
+        bulk_commit();
+        WY_TR(9);
+      }
+    }
+    // the bulk stores have read their shared-memory sources before the CTA goes away
+    if (ptid == 0) bulk_wait_read();
     if (!ok) *abort_flag = 1;
   }
   __syncthreads();
-  if (tid == 128) {
-    if (!*abort_flag) {
-      // the whole packet image -> global in one bulk copy
-      uint8_t* dst = P.packets + (size_t(bh) * P.NS + il) * kPacketBytes;
-      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
-                   "r"(sb + wy::pk), "r"(kPacketBytes)
-                   : "memory");
-      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-    } else {
-      // a failed wait: let the TMA load land before the CTA releases its smem
+  if (warp == 4) {
+    if (lane == 0 && *abort_flag) {
+      // a failed wait: let the TMA loads land before the CTA releases its smem
       volatile int never = 0;
       mbar_wait(&bars[wy::B_FULL], 0, &never);
       if (P.status != nullptr) atomicOr(P.status, 1 << GDN_ERR_TIMEOUT);
     }
-    // every issued MMA completes before TMEM is released
-    mma_commit(&bars[wy::B_DONE]);
-    volatile int never = 0;
-    mbar_wait(&bars[wy::B_DONE], 0, &never);
-  }
-  __syncthreads();
-  if (warp == 4) {
+    __syncwarp();
+    // every issued MMA completes before TMEM is released (same elected lane as the MMAs)
+    mma_commit_warp(&bars[wy::B_DONE]);
+    if (lane == 0) {
+      volatile int never = 0;
+      mbar_wait(&bars[wy::B_DONE], 0, &never);
+    }
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 256);
+    if (lane == 0) WY_TR(12);
+#ifdef GDN_TRACE
+    if (lane == 0 && P.trace != nullptr && blockIdx.x < 64) {
+      long long gt;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
+      P.trace[blockIdx.x * 24 + 21] = gt;
+    }
+#endif
   }
 }
 
 // =========================================================== scan kernel
 namespace sc {
-constexpr int kThreads = 384;
-// stage layout (76 KB): per column block cb: [W16 | q->Qhat | k->Kbar] x 8 KB,
-// then the v slice, then [Tb_hi | P | Tb_lo]
-constexpr uint32_t kStage = 77824;             // 76 KB
-constexpr uint32_t kCb = 24576;                // column-block stride
-constexpr uint32_t kOffQ = 8192, kOffK = 16384;
-constexpr uint32_t kOffV = 49152;              // v slice (4 KB for BV=32)
-constexpr uint32_t kOffTp = 53248;             // [Tb_hi | P | Tb_lo], 24 KB
-constexpr uint32_t st0 = 0, st1 = kStage;
-constexpr uint32_t ht16 = 2 * kStage;          // 155648: h^T fp16, 128 rows x 64 B
-constexpr uint32_t u16 = ht16 + 8192;          // u fp16, 64 rows x 64 B
-constexpr uint32_t vec = u16 + 4096;           // 4 chunks x kVecN x 64 fp32
-constexpr uint32_t bars = vec + 4 * kVecN * kC * 4;
-constexpr uint32_t misc = bars + 32 * 8;
+// warps 0-3: state chain + output rows (TMEM lane quarters), warp 4: ring A loads,
+// warp 5: every tcgen05.mma of the CTA, warp 6: ring B loads
+constexpr int kThreads = 224;
+constexpr int kStages = 3;
+// ring A slot: N (32 KB), free once N S of its chunk completed
+// ring B slot: [Q' 16 KB | hdr] (one bulk copy), this CTA's c and o_intra slices
+constexpr uint32_t kSlotA = 32768;
+constexpr uint32_t kOffQ = 0, kOffHdr = 16384, kOffC = 17408, kOffO = 25600;
+constexpr uint32_t kSlotB = 29696;
+constexpr uint32_t ringA = 0;
+constexpr uint32_t ringB = kStages * kSlotA;
+constexpr int kSBufs = 3;                   // S fp16 [k][v] MN-major SW64, 8 KB each
+constexpr uint32_t s16 = ringB + kStages * kSlotB;
+constexpr uint32_t bars = s16 + kSBufs * 8192;
+constexpr uint32_t misc = bars + 24 * 8;
 constexpr uint32_t total = misc + 32;
 constexpr uint32_t alloc = total + 1024;
 static_assert(alloc <= 232448, "shared memory budget exceeded");
-// TMEM columns (BV = 32)
-constexpr uint32_t kTmU0 = 0, kTmU1 = 32, kTmD1 = 64, kTmD2 = 96, kTmD3 = 128;
+static_assert(kOffO + 4096 <= kSlotB && kOffHdr + 256 <= kOffC && kSlotB % 1024 == 0, "slot layout");
+static_assert(pkt::kQ + 16384 == pkt::kHdr, "Q' and hdr adjacent in the packet");
+constexpr uint32_t kTmN = 0, kTmO = 32;  // N S (M=128, 32 cols); Q' S (M=64) x 2 buffers
 enum {
-  B_FULL = 0,   // [2]
-  B_EMPTY = 2,  // [2]
-  B_VEC = 4,    // [4]
-  B_CVT = 8,    // [2]
-  B_UFULL = 10, // [2]
-  B_UFREE = 12, // [2]
-  B_D1 = 14,
-  B_D2 = 15,
-  B_DONE = 16,   // U issuer drain
-  B_DONE2 = 17,  // chain issuer drain
-  B_COUNT = 18
+  B_FULLA = 0,    // [3] N landed
+  B_FULLB = 3,    // [3] Q', hdr, c, o_intra landed
+  B_EMPTYA = 6,   // [3] N S of the slot's chunk complete (MMA commit)
+  B_EMPTYB = 9,   // [3] output MMA commit + 4 chain warps
+  B_DN = 12,      // N S of the current chunk complete
+  B_DO = 13,      // [2] Q' S of a chunk complete
+  B_SREADY = 15,  // S16 of the next chunk written (4 chain warps)
+  B_DONE = 16,
+  B_COUNT = 17
 };
 }  // namespace sc
 
-template <typename InT, typename OutT>
+// Chunk c's products are issued in the order N S(c), then Q' S(c-1): the chain
+// product never queues behind an output product, and the output product of
+// chunk c-1 runs while the chain warps update the state with N S(c).
+template <typename OutT>
 __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_constant__ ScanParams P) {
   constexpr int BV = 32;
   extern __shared__ uint8_t smem_raw[];
@@ -318,7 +561,6 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + sc::bars);
   uint32_t* tmem_base_p = reinterpret_cast<uint32_t*>(sm + sc::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + sc::misc + 4);
-  float* vecs = reinterpret_cast<float*>(sm + sc::vec);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int NT = P.NS;
   const int slice = blockIdx.x % P.nslice;
@@ -328,271 +570,209 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
   const uint32_t sb = smem_u32(sm);
 
   if (tid == 0) {
-    const uint32_t counts[sc::B_COUNT] = {1, 1, 2, 2, 32, 32, 32, 32, 4, 4, 1, 1, 2, 2, 1, 1, 1, 1};
-    for (int i = 0; i < sc::B_COUNT; ++i) mbar_init(&bars[i], counts[i]);
+    for (int i = 0; i < sc::B_COUNT; ++i) {
+      const bool emptyb = i >= sc::B_EMPTYB && i < sc::B_EMPTYB + 3;
+      mbar_init(&bars[i], emptyb ? 5 : (i == sc::B_SREADY ? 4 : 1));
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
-    prefetch_tmap(&P.tm_q);
-    prefetch_tmap(&P.tm_k);
-    prefetch_tmap(&P.tm_v);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_base_p, 256);
+  if (warp == 4) {
+    tmem_alloc(tmem_base_p, 128);
     tmem_relinquish();
   }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base_p;
-  auto stage = [&](int i) -> uint32_t { return (i & 1) ? sc::st1 : sc::st0; };
 
-  if (warp == 0) {
-    // ================================================================ producer
-    constexpr float kLog2e = 1.4426950408889634f;
-    const float* gp = P.g + bb * P.sg_b + hh * P.sg_h;
+  if (warp == 4 || warp == 6) {
+    // ================================================================ producers (ring A: N, ring B: the rest)
+    const bool ra = warp == 4;
+    const int fullb = ra ? sc::B_FULLA : sc::B_FULLB;
+    const int emptyb = ra ? sc::B_EMPTYA : sc::B_EMPTYB;
     int issued = 0;
     for (int i = 0; i < NT; ++i) {
-      const int s = i & 1;
-      if (i >= 2 && !mbar_wait_warp(&bars[sc::B_EMPTY + s], ((i >> 1) - 1) & 1, abort_flag)) break;
-      const int t0 = (P.c0 + i) * kC;
+      const int s = i % sc::kStages;
+      if (i >= sc::kStages && !mbar_wait_warp(&bars[emptyb + s], ((i / sc::kStages) - 1) & 1, abort_flag)) break;
       if (lane == 0) {
-        uint8_t* st = sm + stage(i);
-        uint64_t* fb = &bars[sc::B_FULL + s];
-        mbar_arrive_expect_tx(fb, 32768 + 4096 + kPacketBytes);
-        tma_load_4d(st + sc::kOffQ, &P.tm_q, fb, 0, t0, hh, bb);
-        tma_load_4d(st + sc::kOffK, &P.tm_k, fb, 0, t0, hh, bb);
-        tma_load_4d(st + sc::kCb + sc::kOffQ, &P.tm_q, fb, 64, t0, hh, bb);
-        tma_load_4d(st + sc::kCb + sc::kOffK, &P.tm_k, fb, 64, t0, hh, bb);
-        tma_load_4d(st + sc::kOffV, &P.tm_v, fb, v0, t0, hh, bb);
+        uint64_t* fb = &bars[fullb + s];
         const uint8_t* pk = P.packets + (size_t(bh) * P.NS + i) * kPacketBytes;
-        const uint32_t fbs = smem_u32(fb);
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                smem_u32(st)),
-            "l"(pk + kPkW0), "r"(8192u), "r"(fbs)
-            : "memory");
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                smem_u32(st + sc::kCb)),
-            "l"(pk + kPkW1), "r"(8192u), "r"(fbs)
-            : "memory");
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                smem_u32(st + sc::kOffTp)),
-            "l"(pk + kPkTbHi), "r"(24576u), "r"(fbs)
-            : "memory");
-      }
-      issued = i + 1;
-      const int ta = t0 + lane, tb = t0 + lane + 32;
-      float xa = (ta < P.T) ? gp[(long long)ta * P.sg_t] * kLog2e : 0.f;
-      float xb = (tb < P.T) ? gp[(long long)tb * P.sg_t] * kLog2e : 0.f;
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const float ya = __shfl_up_sync(0xffffffffu, xa, d);
-        const float yb = __shfl_up_sync(0xffffffffu, xb, d);
-        if (lane >= d) {
-          xa += ya;
-          xb += yb;
+        if (ra) {
+          mbar_arrive_expect_tx(fb, 32768);
+          bulk_load(sm + sc::ringA + s * sc::kSlotA, pk + pkt::kN, 32768, fb);
+          GDN_TR(0, i);
+          // ring B is freed a chunk later than ring A: pull its pieces of chunk
+          // i + 2 (and the N of chunk i + 3) into L2 now, so its loads hit L2
+          if (i + 2 < NT) {
+            const uint8_t* pf = pk + 2 * size_t(kPacketBytes);
+            bulk_prefetch_l2(pf + pkt::kQ, 16640);
+            bulk_prefetch_l2(pf + pkt::kCs + slice * 8192, 8192);
+            bulk_prefetch_l2(pf + pkt::kOs + slice * 4096, 4096);
+          }
+          if (i + 3 < NT) bulk_prefetch_l2(pk + 3 * size_t(kPacketBytes) + pkt::kN, 32768);
+        } else {
+          uint8_t* st = sm + sc::ringB + s * sc::kSlotB;
+          mbar_arrive_expect_tx(fb, 16640 + 8192 + 4096);
+          bulk_load(st + sc::kOffQ, pk + pkt::kQ, 16640, fb);
+          bulk_load(st + sc::kOffC, pk + pkt::kCs + slice * 8192, 8192, fb);
+          bulk_load(st + sc::kOffO, pk + pkt::kOs + slice * 4096, 4096, fb);
         }
       }
-      xb += __shfl_sync(0xffffffffu, xa, 31);
-      const float bC = __shfl_sync(0xffffffffu, xb, 31);
-      // vec[i & 3] is free: chunk i-4's readers finished before EMPTY(i-2) completed
-      float* vec = vecs + (i & 3) * kVecN * kC;
-      vec[V_B2 * kC + lane] = xa;
-      vec[V_B2 * kC + lane + 32] = xb;
-      vec[V_EB * kC + lane] = fast_exp2(xa);
-      vec[V_EB * kC + lane + 32] = fast_exp2(xb);
-      vec[V_DD * kC + lane] = fast_exp2(bC - xa);
-      vec[V_DD * kC + lane + 32] = fast_exp2(bC - xb);
-      mbar_arrive(&bars[sc::B_VEC + (i & 3)]);
+      issued = i + 1;
     }
     if (lane == 0) {
+      // let every issued copy land before the CTA exits
       volatile int never = 0;
-      for (int i = (issued > 2 ? issued - 2 : 0); i < issued; ++i)
-        mbar_wait(&bars[sc::B_FULL + (i & 1)], (i >> 1) & 1, &never);
+      for (int i = (issued > sc::kStages ? issued - sc::kStages : 0); i < issued; ++i)
+        mbar_wait(&bars[fullb + i % sc::kStages], (i / sc::kStages) & 1, &never);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ================================================================ U = Tb V
-    if (lane == 0) {
-      constexpr uint32_t kInBf16 = Cvt<InT>::kIsBf16;
-      const uint32_t id_u = idesc_f16(128, BV, kInBf16, 0, 1);
-      bool okm = true;
-      for (int i = 0; i < NT && okm; ++i) {
-        const int s = i & 1;
-        okm = mbar_wait(&bars[sc::B_FULL + s], (i >> 1) & 1, abort_flag) &&
-              (i < 2 || mbar_wait(&bars[sc::B_UFREE + s], ((i >> 1) - 1) & 1, abort_flag));
-        if (!okm) break;
-        tc_fence_after();
-        const uint32_t tp = sb + stage(i) + sc::kOffTp;
-        const uint32_t vt = sb + stage(i) + sc::kOffV;
-        // rows 0-63 of A: Tb_hi (k-steps 0-3), Tb_lo (k-steps 4-7); U lands in lanes 0-63
+  } else if (warp == 5) {
+    // ================================================================ MMA issue (whole warp, elect.sync)
+    const uint32_t id_n = idesc_f16(128, BV, 0, 0, 1);
+    const uint32_t id_o = idesc_f16(64, BV, 0, 0, 1);
+    auto issue_out = [&](int c) -> bool {
+      const int s = c % sc::kStages;
+      if (!mbar_wait_warp(&bars[sc::B_FULLB + s], (c / sc::kStages) & 1, abort_flag)) return false;
+      tc_fence_after();
+      const uint32_t st = sb + sc::ringB + s * sc::kSlotB;
+      const uint32_t sbuf = sb + sc::s16 + (c % sc::kSBufs) * 8192;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ss(tmem + (s ? sc::kTmU1 : sc::kTmU0),
-                     sdesc(tp + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSw128),
-                     sdesc(vt + (kk & 3) * 1024, 8192, 512, kSw64), id_u, kk > 0);
-        mma_commit(&bars[sc::B_UFULL + s]);
-        mma_commit(&bars[sc::B_EMPTY + s]);
-      }
-      if (!okm) *abort_flag = 1;
-      mma_commit(&bars[sc::B_DONE]);
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_ss_warp(tmem + sc::kTmO + (c & 1) * BV,
+                        sdesc(st + sc::kOffQ + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024, kSw128),
+                        sdesc(sbuf + kk * 1024, 8192, 512, kSw64), id_o, kk > 0);
+      mma_commit_warp(&bars[sc::B_DO + (c & 1)]);
+      mma_commit_warp(&bars[sc::B_EMPTYB + s]);
+      return true;
+    };
+    bool okm = true;
+    for (int c = 0; c < NT && okm; ++c) {
+      const int s = c % sc::kStages;
+      okm = mbar_wait_warp(&bars[sc::B_FULLA + s], (c / sc::kStages) & 1, abort_flag);
+      if (lane == 0) GDN_TR(5, c);
+      okm = okm && mbar_wait_warp(&bars[sc::B_SREADY], c & 1, abort_flag);
+      if (!okm) break;
+      tc_fence_after();
+      if (lane == 0) GDN_TR(1, c);
+      const uint32_t st = sb + sc::ringA + s * sc::kSlotA;
+      const uint32_t sbuf = sb + sc::s16 + (c % sc::kSBufs) * 8192;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_ss_warp(tmem + sc::kTmN, sdesc(st + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSw128),
+                        sdesc(sbuf + kk * 1024, 8192, 512, kSw64), id_n, kk > 0);
+      mma_commit_warp(&bars[sc::B_DN]);
+      mma_commit_warp(&bars[sc::B_EMPTYA + s]);
+      if (lane == 0) GDN_TR(6, c);
+      if (c > 0) okm = issue_out(c - 1);
+      if (lane == 0) GDN_TR(7, c);
+    }
+    if (okm && NT > 0) okm = issue_out(NT - 1);
+    if (!okm && lane == 0) *abort_flag = 1;
+    // issued MMAs complete before TMEM is released (same elected lane as the MMAs)
+    mma_commit_warp(&bars[sc::B_DONE]);
+    if (lane == 0) {
       volatile int never = 0;
       mbar_wait(&bars[sc::B_DONE], 0, &never);
     }
     __syncwarp();
-  } else if (warp >= 4 && warp < 8) {
-    // ================================================================ convert in place
-    // thread: row r of q (half 0) or of k (half 1); Qhat = e^{b_t} q_t, Kbar = e^{b_C - b_t} k_t (fp16)
-    const int ct = tid - 128, r = ct & 63, isk = ct >> 6;
-    for (int i = 0; i < NT; ++i) {
-      const int s = i & 1;
-      if (!mbar_wait_warp(&bars[sc::B_FULL + s], (i >> 1) & 1, abort_flag)) break;
-      if (!mbar_wait_warp(&bars[sc::B_VEC + (i & 3)], (i >> 2) & 1, abort_flag)) break;
-      const float* vec = vecs + (i & 3) * kVecN * kC;
-      const float sc_ = isk ? vec[V_DD * kC + r] : vec[V_EB * kC + r];
-      uint8_t* base = sm + stage(i) + (isk ? sc::kOffK : sc::kOffQ);
-#pragma unroll 1
-      for (int cc = 0; cc < 16; ++cc) {
-        uint8_t* p = base + (cc >> 3) * sc::kCb + sw128_off(r, cc & 7);
-        const uint4 x = *reinterpret_cast<const uint4*>(p);
-        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-        uint32_t ys[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = Cvt<InT>::unpack(xs[e]);
-          ys[e] = Cvt<__half>::pack(f.x * sc_, f.y * sc_);
-        }
-        *reinterpret_cast<uint4*>(p) = make_uint4(ys[0], ys[1], ys[2], ys[3]);
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[sc::B_CVT + s]);
-    }
-  } else if (warp >= 8) {
-    // ================================================================ chain
-    // Thread r owns row d = r of h^T in fp32 registers (TMEM lane r).
-    //   D1 = [W; Qhat] h^T   lanes 0-63: W h^T, lanes 64-127: Qhat h^T   (issued by r = 0)
-    //   u  = U - W h^T       (U in lanes 0-63)
-    //   D2 = Kbar^T u, D3 = [* ; P] u  (P u in lanes 64-127)            (issued by r = 0)
-    //   h  = e^{b_C} h + D2,  o = Qhat h^T + P u
-    const int r = tid - 256;
-    const int wq = warp - 8;
-    const uint32_t id_1 = idesc_f16(128, BV, 0, 0, 1);
-    const uint32_t id_2 = idesc_f16(128, BV, 0, 1, 1);
-    float h[BV];
+  } else {
+    // ================================================================ chain (thread r = row k of S)
+    const int r = tid;
     const size_t hbase = (size_t(bb) * P.H + hh) * kV * kK;
+    float S[BV];
     if (P.h0 != nullptr) {
 #pragma unroll
-      for (int j = 0; j < BV; ++j) h[j] = P.h0[hbase + size_t(v0 + j) * kK + r];
+      for (int j = 0; j < BV; ++j) S[j] = P.h0[hbase + size_t(v0 + j) * kK + r];
     } else {
 #pragma unroll
-      for (int j = 0; j < BV; ++j) h[j] = 0.f;
+      for (int j = 0; j < BV; ++j) S[j] = 0.f;
     }
-    bool ok = true;
-    auto issue_d1 = [&](int c) -> bool {
-      const int s = c & 1;
-      if (!mbar_wait(&bars[sc::B_FULL + s], (c >> 1) & 1, abort_flag)) return false;
-      if (!mbar_wait(&bars[sc::B_CVT + s], (c >> 1) & 1, abort_flag)) return false;
+    // output rows of chunk c: o = Q' S + o_intra (gdn_ref.py:86-90); rows t = 16 w + l (l < 16)
+    auto out_rows = [&](int c) -> bool {
+      const int s = c % sc::kStages;
+      if (!mbar_wait_warp(&bars[sc::B_DO + (c & 1)], (c >> 1) & 1, abort_flag)) return false;
       tc_fence_after();
-      const uint32_t st = sb + stage(c);
+      float ov[BV];
+      tmem_ld32w(tmem_addr(tmem + sc::kTmO + (c & 1) * BV, warp * 32, 0), ov);
+      tc_fence_before();
+      const int t = 16 * warp + lane;
+      const int tg = (P.c0 + c) * kC + t;
+      const uint8_t* st = sm + sc::ringB + s * sc::kSlotB;
+      if (lane < 16 && tg < P.T) {
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss(tmem + sc::kTmD1, sdesc(st + (kk >> 2) * sc::kCb + (kk & 3) * 32, 16, 1024, kSw128),
-                   sdesc(sb + sc::ht16 + kk * 1024, 8192, 512, kSw64), id_1, kk > 0);
-      mma_commit(&bars[sc::B_D1]);
+        for (int q = 0; q < 4; ++q) {
+          const uint4 x = *reinterpret_cast<const uint4*>(st + sc::kOffO + sw64_off(t, q));
+          const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = Cvt<__half>::unpack(xs[e]);
+            ov[8 * q + 2 * e] += f.x;
+            ov[8 * q + 2 * e + 1] += f.y;
+          }
+        }
+        OutT* dst = reinterpret_cast<OutT*>(P.o) + bb * P.so_b + (long long)tg * P.so_t + hh * P.so_h + v0;
+        store_row<OutT>(dst, ov, BV);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[sc::B_EMPTYB + s]);
       return true;
     };
-    st_row16<BV>(sm + sc::ht16, r, 0, h);
+    st_row16<BV>(sm + sc::s16, r, 0, S);
     fence_async_smem();
-    if (!bar_any(3, 128, false) && r == 0 && NT > 0) {
-      if (!issue_d1(0)) *abort_flag = 1;
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars[sc::B_SREADY]);
+    bool ok = true;
     for (int i = 0; i < NT; ++i) {
-      const int s = i & 1;
-      ok = mbar_wait_warp(&bars[sc::B_D1], i & 1, abort_flag);
-      if (ok) tc_fence_after();
-      float y[BV];
-      if (r < 64) {
-        ok = ok && mbar_wait_warp(&bars[sc::B_UFULL + s], (i >> 1) & 1, abort_flag);
-        if (ok) {
-          tc_fence_after();
-          float x[BV], uu[BV];
-          tmem_ld32w(tmem_addr(tmem + sc::kTmD1, wq * 32, 0), x);
-          tmem_ld32w(tmem_addr(tmem + (s ? sc::kTmU1 : sc::kTmU0), wq * 32, 0), uu);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars[sc::B_UFREE + s]);
+      const int s = i % sc::kStages;
+      const uint8_t* st = sm + sc::ringB + s * sc::kSlotB;
+      ok = mbar_wait_warp(&bars[sc::B_FULLB + s], (i / sc::kStages) & 1, abort_flag);
+      if (!ok) break;
+      float cv[BV];
 #pragma unroll
-          for (int j = 0; j < BV; ++j) uu[j] -= x[j];  // u = U - W h^T   (gdn_ref.py:86)
-          st_row16<BV>(sm + sc::u16, r, 0, uu);
-          fence_async_smem();
+      for (int q = 0; q < 4; ++q) {
+        const uint4 x = *reinterpret_cast<const uint4*>(st + sc::kOffC + sw64_off(r, q));
+        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = Cvt<__half>::unpack(xs[e]);
+          cv[8 * q + 2 * e] = f.x;
+          cv[8 * q + 2 * e + 1] = f.y;
         }
-        if (!bar_any(4, 64, !ok) && r == 0) {
-          tc_fence_after();
-          const uint32_t st = sb + stage(i);
-          const uint32_t tp = st + sc::kOffTp;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f16_ss(tmem + sc::kTmD2, sdesc(st + sc::kOffK + kk * 2048, sc::kCb, 1024, kSw128),
-                       sdesc(sb + sc::u16 + kk * 1024, 8192, 512, kSw64), id_2, kk > 0);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f16_ss(tmem + sc::kTmD3, sdesc(tp + kk * 32, 16, 1024, kSw128),
-                       sdesc(sb + sc::u16 + kk * 1024, 8192, 512, kSw64), id_1, kk > 0);
-          mma_commit(&bars[sc::B_D2]);
-          mma_commit(&bars[sc::B_EMPTY + s]);
-        }
-      } else if (ok) {
-        tmem_ld32w(tmem_addr(tmem + sc::kTmD1, wq * 32, 0), y);
       }
-      ok = ok && mbar_wait_warp(&bars[sc::B_D2], i & 1, abort_flag) &&
-           mbar_wait_warp(&bars[sc::B_VEC + (i & 3)], (i >> 2) & 1, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        float dh[BV];
-        tmem_ld32w(tmem_addr(tmem + sc::kTmD2, wq * 32, 0), dh);
-        const float gam = vecs[(i & 3) * kVecN * kC + V_EB * kC + kC - 1];  // e^{b_C}
+      const float gam = *reinterpret_cast<const float*>(st + sc::kOffHdr);
+      ok = mbar_wait_warp(&bars[sc::B_DN], i & 1, abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      if (r == 0) GDN_TR(2, i);
+      float d[BV];
+      tmem_ld32w(tmem_addr(tmem + sc::kTmN, warp * 32, 0), d);
+      tc_fence_before();
+      // S' = e^{b_C} S + N S + c   (gdn_ref.py:92-98, regrouped)
 #pragma unroll
-        for (int j = 0; j < BV; ++j) h[j] = fmaf(gam, h[j], dh[j]);  // h' = e^{b_C} h + Kbar^T u
-        if (i + 1 < NT) st_row16<BV>(sm + sc::ht16, r, 0, h);
-        float z[BV];
-        tmem_ld32w(tmem_addr(tmem + sc::kTmD3, wq * 32, 0), z);
-        const int t = (P.c0 + i) * kC + (r - 64);
-        if (r >= 64 && t < P.T) {
-#pragma unroll
-          for (int j = 0; j < BV; ++j) z[j] += y[j];  // o = Qhat h^T + P u   (gdn_ref.py:89-90)
-          OutT* dst = reinterpret_cast<OutT*>(P.o) + bb * P.so_b + (long long)t * P.so_t + hh * P.so_h + v0;
-          store_row<OutT>(dst, z, BV);
-        }
-        tc_fence_before();
+      for (int j = 0; j < BV; ++j) S[j] = fmaf(gam, S[j], d[j] + cv[j]);
+      if (i + 1 < NT) {
+        st_row16<BV>(sm + sc::s16 + ((i + 1) % sc::kSBufs) * 8192, r, 0, S);
         fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[sc::B_SREADY]);
       }
-      if (bar_any(3, 128, !ok || *abort_flag)) {
-        ok = false;
-        break;
-      }
-      if (r == 0 && i + 1 < NT && !issue_d1(i + 1)) *abort_flag = 1;
+      if (r == 0) GDN_TR(3, i);
+      if (i > 0 && !(ok = out_rows(i - 1))) break;
+      if (r == 0) GDN_TR(4, i);
     }
+    if (ok && NT > 0) ok = out_rows(NT - 1);
     if (ok && P.ht != nullptr) {
 #pragma unroll
-      for (int j = 0; j < BV; ++j) P.ht[hbase + size_t(v0 + j) * kK + r] = h[j];
+      for (int j = 0; j < BV; ++j) P.ht[hbase + size_t(v0 + j) * kK + r] = S[j];
     }
     if (!ok) *abort_flag = 1;
-    if (r == 0) {
-      // chain MMAs complete before TMEM is released
-      mma_commit(&bars[sc::B_DONE2]);
-      volatile int never = 0;
-      mbar_wait(&bars[sc::B_DONE2], 0, &never);
-    }
   }
   __syncthreads();
   if (*abort_flag && tid == 0 && P.status != nullptr) atomicOr(P.status, 1 << GDN_ERR_TIMEOUT);
-  if (warp == 1) {
+  if (warp == 4) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 128);
   }
 }
 
@@ -612,9 +792,9 @@ int launch_wy(const WyParams& p, int grid, cudaStream_t s) {
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
 
-template <typename InT, typename OutT>
+template <typename OutT>
 int launch_scan(const ScanParams& p, int grid, cudaStream_t s) {
-  auto kern = gdn_scan_kernel<InT, OutT>;
+  auto kern = gdn_scan_kernel<OutT>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -631,15 +811,10 @@ int run_wy(int in_bf16, const WyParams& p, int grid, cudaStream_t s) {
   return in_bf16 ? launch_wy<__nv_bfloat16>(p, grid, s) : launch_wy<__half>(p, grid, s);
 }
 
-int run_scan(int in_bf16, int out_dtype, const ScanParams& p, int grid, cudaStream_t s) {
-  if (in_bf16) {
-    if (out_dtype == GDN_DTYPE_F32) return launch_scan<__nv_bfloat16, float>(p, grid, s);
-    if (out_dtype == GDN_DTYPE_F16) return launch_scan<__nv_bfloat16, __half>(p, grid, s);
-    return launch_scan<__nv_bfloat16, __nv_bfloat16>(p, grid, s);
-  }
-  if (out_dtype == GDN_DTYPE_F32) return launch_scan<__half, float>(p, grid, s);
-  if (out_dtype == GDN_DTYPE_F16) return launch_scan<__half, __half>(p, grid, s);
-  return launch_scan<__half, __nv_bfloat16>(p, grid, s);
+int run_scan(int out_dtype, const ScanParams& p, int grid, cudaStream_t s) {
+  if (out_dtype == GDN_DTYPE_F32) return launch_scan<float>(p, grid, s);
+  if (out_dtype == GDN_DTYPE_F16) return launch_scan<__half>(p, grid, s);
+  return launch_scan<__nv_bfloat16>(p, grid, s);
 }
 
 }  // namespace gdn

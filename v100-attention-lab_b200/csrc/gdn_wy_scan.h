@@ -6,35 +6,36 @@
 
 namespace gdn {
 
+// Chunk-parallel prep: reads q, k, v (TMA, 64-column boxes, 128B swizzle),
+// beta and g; writes one packet per (b, h, chunk).
 struct WyParams {
-  CUtensorMap tm_q, tm_k;
+  CUtensorMap tm_q, tm_k, tm_v;
   const float* beta;
   const float* g;
-  uint8_t* packets;  // NS packets of 40 KB per (b, h)
+  uint8_t* packets;  // NS packets per (b, h)
   int* status;
+  long long* trace;  // GDN_TRACE builds: phase timestamps of CTAs 0-63
   long long sb_b, sb_t, sb_h;
   long long sg_b, sg_t, sg_h;
   int B, T, H, c0, NS;  // segment = chunks [c0, c0 + NS)
 };
 
+// Serial scan over the packets of one segment.
 struct ScanParams {
-  CUtensorMap tm_q, tm_k, tm_v;
-  const float* beta;
-  const float* g;
-  const float* h0;
-  float* ht;
+  const float* h0;   // state at the segment start [B, H, V, K] fp32, or NULL (zeros)
+  float* ht;         // state at the segment end, same layout (may alias h0)
   void* o;
   const uint8_t* packets;
   int* status;
-  long long sb_b, sb_t, sb_h;
-  long long sg_b, sg_t, sg_h;
+  long long* trace;  // GDN_TRACE builds: per-chunk role timestamps of CTA 0
   long long so_b, so_t, so_h;
   int B, T, H, c0, NS, nslice;
 };
 
-constexpr uint64_t kPacketBytesPerChunk = 40960;
+// Bytes of one packet: N and Q' images, e^{b_C}, c and o_intra slices (fp16).
+constexpr uint64_t kPacketBytesPerChunk = 98560;
 
 int run_wy(int in_bf16, const WyParams& p, int grid, cudaStream_t s);
-int run_scan(int in_bf16, int out_dtype, const ScanParams& p, int grid, cudaStream_t s);
+int run_scan(int out_dtype, const ScanParams& p, int grid, cudaStream_t s);
 
 }  // namespace gdn

@@ -27,6 +27,10 @@ ERR_TIMEOUT = 5
 ERR_NO_DEVICE = 6
 ERR_SCRATCH_LIMIT = 7
 
+# Scratch bytes of the two-kernel path per (batch, head, chunk of 64 steps);
+# gdn_fwd_workspace_bytes() is the authority, this mirrors it for sizing.
+PACKET_BYTES_PER_CHUNK = 98560
+
 # Every symbol include/gdn_b200.h declares.
 EXPORTED_SYMBOLS = ("gdn_fwd_sm100", "gdn_fwd_sm100_noalloc", "gdn_fwd_workspace_bytes", "gdn_wy_prep_sm100",
                     "gdn_selftest_wait_timeout", "gdn_status_string", "gdn_abi_version")

@@ -172,7 +172,7 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
     args = _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status)
     if not fused:
         need = int(lib.gdn_fwd_workspace_bytes(ctypes.byref(args)))
-        per_head = B * H * (40960 + V * K * 4)
+        per_head = B * H * (_lib.PACKET_BYTES_PER_CHUNK + V * K * 4)
         nbytes = max(min(need, WORKSPACE_CAP_BYTES), per_head)
         ws = _workspace(dev, nbytes)
         args.workspace = ws.data_ptr()
