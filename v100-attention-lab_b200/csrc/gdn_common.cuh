@@ -90,67 +90,120 @@ __device__ __forceinline__ void st_row16(uint8_t* tile, uint32_t r, uint32_t c16
 // diagonal blocks are inverted by column forward substitution; three
 // doubling levels (8 -> 16 -> 32 -> 64) then apply
 //     inv([[L0, 0], [X, L1]]) = [[inv(L0), 0], [-inv(L1) X inv(L0), inv(L1)]].
-// The upper triangle of every block stays zero, so the block products can run
-// over full index ranges.  Same result as the row-by-row forward substitution
-// of gdn_triton.py:75-84 applied to the identity.
+// The upper triangle of every block stays zero (the triangular factors' zero
+// halves are skipped, not read).  Same result as the row-by-row forward
+// substitution of gdn_triton.py:75-84 applied to the identity.
+// Work items of one doubling level are 1 x 4 output strips (blk, row i, strip q).
+// Phase 1 sums over m >= 4q only (inv(L0) is lower triangular), phase 2 over
+// p <= i only (inv(L1) likewise); items are paired (q with N/4-1-q, i with
+// N-1-i) so that every lane of a warp runs the same number of iterations.
+template <int N>
+struct InvItems {
+  static constexpr int NB = 64 / (2 * N), NQ = N / 4;
+  static constexpr int PER = (NB * N * NQ + 127) / 128;  // items per thread (1 or 2)
+  __device__ static bool p1(int tid, int e, int& blk, int& i, int& q) {
+    if constexpr (N == 32) {
+      blk = 0; i = tid & 31; q = e == 0 ? (tid >> 5) : NQ - 1 - (tid >> 5);
+      return true;
+    } else if constexpr (N == 16) {
+      blk = tid >> 6; i = tid & 15; q = (tid >> 4) & 3;
+      return true;
+    } else {
+      blk = tid >> 4; i = tid & 7; q = (tid >> 3) & 1;
+      return tid < 64;
+    }
+  }
+  __device__ static bool p2(int tid, int e, int& blk, int& i, int& q) {
+    if constexpr (N == 32) {
+      blk = 0; q = tid & 7; i = e == 0 ? (tid >> 3) : N - 1 - (tid >> 3);
+      return true;
+    } else if constexpr (N == 16) {
+      blk = tid >> 6; q = tid & 3; i = (tid >> 2) & 15;
+      return true;
+    } else {
+      blk = tid >> 4; q = tid & 1; i = (tid >> 1) & 7;
+      return tid < 64;
+    }
+  }
+};
+
+__device__ __forceinline__ void fma4(float4& acc, float a, const float4& b) {
+  acc.x = fmaf(a, b.x, acc.x);
+  acc.y = fmaf(a, b.y, acc.y);
+  acc.z = fmaf(a, b.z, acc.z);
+  acc.w = fmaf(a, b.w, acc.w);
+}
+
 template <int N>
 __device__ __forceinline__ void inv_level(float* am, int tid) {
-  constexpr int NTH = 128;
-  constexpr int NOUT = (64 / (2 * N)) * N * N;  // outputs per phase
-  constexpr int PER = NOUT / NTH;               // outputs per thread
-  float acc[PER];
-  // phase 1: Y = X inv(L0), X = rows N..2N-1 x cols 0..N-1 of each 2N block
+  using It = InvItems<N>;
+  constexpr int S = kAStride;
+  float4 acc[It::PER];
+  // phase 1: Y = X inv(L0); X = rows N..2N-1 x cols 0..N-1 of each 2N block
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NTH;
-    const int pr = idx / (N * N), rem = idx % (N * N);
-    const int i = rem / N, j = rem % N, o = pr * 2 * N;
-    const float* xr = am + (o + N + i) * kAStride + o;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  for (int e = 0; e < It::PER; ++e) {
+    int blk, i, q;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    if (It::p1(tid, e, blk, i, q)) {
+      const int o = blk * 2 * N;
+      const float* xr = am + (o + N + i) * S + o;
 #pragma unroll
-    for (int m = 0; m < N; m += 4) {
-      const float4 xv = *reinterpret_cast<const float4*>(xr + m);
-      s0 = fmaf(xv.x, am[(o + m + 0) * kAStride + o + j], s0);
-      s1 = fmaf(xv.y, am[(o + m + 1) * kAStride + o + j], s1);
-      s2 = fmaf(xv.z, am[(o + m + 2) * kAStride + o + j], s2);
-      s3 = fmaf(xv.w, am[(o + m + 3) * kAStride + o + j], s3);
+      for (int m4 = 0; m4 < It::NQ; ++m4) {
+        if (m4 >= q) {
+          const float4 x = *reinterpret_cast<const float4*>(xr + 4 * m4);
+          const float* t0 = am + (o + 4 * m4) * S + o + 4 * q;
+          fma4(a0, x.x, *reinterpret_cast<const float4*>(t0));
+          fma4(a1, x.y, *reinterpret_cast<const float4*>(t0 + S));
+          fma4(a0, x.z, *reinterpret_cast<const float4*>(t0 + 2 * S));
+          fma4(a1, x.w, *reinterpret_cast<const float4*>(t0 + 3 * S));
+        }
+      }
     }
-    acc[e] = (s0 + s1) + (s2 + s3);
+    acc[e] = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
   }
-  named_bar(1, NTH);
+  named_bar(1, 128);
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NTH;
-    const int pr = idx / (N * N), rem = idx % (N * N);
-    am[(pr * 2 * N + N + rem / N) * kAStride + pr * 2 * N + rem % N] = acc[e];
+  for (int e = 0; e < It::PER; ++e) {
+    int blk, i, q;
+    if (It::p1(tid, e, blk, i, q)) {
+      const int o = blk * 2 * N;
+      *reinterpret_cast<float4*>(am + (o + N + i) * S + o + 4 * q) = acc[e];
+    }
   }
-  named_bar(1, NTH);
+  named_bar(1, 128);
   // phase 2: T = -inv(L1) Y
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NTH;
-    const int pr = idx / (N * N), rem = idx % (N * N);
-    const int i = rem / N, j = rem % N, o = pr * 2 * N;
-    const float* tr = am + (o + N + i) * kAStride + o + N;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  for (int e = 0; e < It::PER; ++e) {
+    int blk, i, q;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    if (It::p2(tid, e, blk, i, q)) {
+      const int o = blk * 2 * N;
+      const float* tr = am + (o + N + i) * S + o + N;
 #pragma unroll
-    for (int p = 0; p < N; p += 4) {
-      const float4 tv = *reinterpret_cast<const float4*>(tr + p);
-      s0 = fmaf(tv.x, am[(o + N + p + 0) * kAStride + o + j], s0);
-      s1 = fmaf(tv.y, am[(o + N + p + 1) * kAStride + o + j], s1);
-      s2 = fmaf(tv.z, am[(o + N + p + 2) * kAStride + o + j], s2);
-      s3 = fmaf(tv.w, am[(o + N + p + 3) * kAStride + o + j], s3);
+      for (int p4 = 0; p4 < It::NQ; ++p4) {
+        if (p4 <= (i >> 2)) {
+          const float4 t = *reinterpret_cast<const float4*>(tr + 4 * p4);
+          const float* y = am + (o + N + 4 * p4) * S + o + 4 * q;
+          fma4(a0, t.x, *reinterpret_cast<const float4*>(y));
+          fma4(a1, t.y, *reinterpret_cast<const float4*>(y + S));
+          fma4(a0, t.z, *reinterpret_cast<const float4*>(y + 2 * S));
+          fma4(a1, t.w, *reinterpret_cast<const float4*>(y + 3 * S));
+        }
+      }
     }
-    acc[e] = -((s0 + s1) + (s2 + s3));
+    acc[e] = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
   }
-  named_bar(1, NTH);
+  named_bar(1, 128);
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NTH;
-    const int pr = idx / (N * N), rem = idx % (N * N);
-    am[(pr * 2 * N + N + rem / N) * kAStride + pr * 2 * N + rem % N] = acc[e];
+  for (int e = 0; e < It::PER; ++e) {
+    int blk, i, q;
+    if (It::p2(tid, e, blk, i, q)) {
+      const int o = blk * 2 * N;
+      *reinterpret_cast<float4*>(am + (o + N + i) * S + o + 4 * q) =
+          make_float4(-acc[e].x, -acc[e].y, -acc[e].z, -acc[e].w);
+    }
   }
-  named_bar(1, NTH);
+  named_bar(1, 128);
 }
 
 __device__ __forceinline__ void invert_unit_lower64(float* am, int ptid) {

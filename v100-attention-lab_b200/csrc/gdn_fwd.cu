@@ -799,6 +799,12 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
   wp.T = sp.T = a->T;
   wp.H = sp.H = a->H;
   sp.nslice = kV / BV;
+  {
+    int dev = 0, nsm = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      wp.pf_stride = 2 * nsm;
+  }
 #ifdef GDN_TRACE
   sp.trace = g_trace;
   wp.trace = g_trace_wy;

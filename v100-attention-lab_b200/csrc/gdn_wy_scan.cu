@@ -52,23 +52,26 @@ static_assert(kOs + 4 * 4096 == kPacketBytesPerChunk, "packet size");
 // =========================================================== prep kernel
 namespace wy {
 constexpr int kThreads = 160;      // warps 0-3: prep (TMEM lanes 0-127), warp 4: TMA + MMA
-constexpr uint32_t kq = 0;         // [k0 | q0 | k1 | q1] 8 KB each (k later -> Kbar fp16 in place)
-constexpr uint32_t vt = 32768;     // [v0 | v1] 8 KB each, later U_hi fp16
-constexpr uint32_t amat = 49152;   // fp32 A / T (64 x kAStride), later W fp16 [w0 | w1]
-constexpr uint32_t tw = 66560;     // Tw (input dtype), 64 x 128 B
-constexpr uint32_t tb = 74752;     // Tb_hi | Tb_lo (input dtype), later U_lo fp16
-constexpr uint32_t p16 = 91136;    // P fp16, 64 x 128 B
-constexpr uint32_t vec = 99328;    // kVecN x 64 fp32
+// Column blocks of 64 elements (128-byte rows, 128B swizzle).  k0, k1, v0, v1
+// sit 16 KB apart so that [K | V] is one N = 256 MN-major operand.
+constexpr uint32_t k0 = 0, q0 = 8192, k1 = 16384, q1 = 24576;  // k later -> Kbar fp16 in place
+constexpr uint32_t v0 = 32768, v1 = 49152;                     // later U_lo fp16
+constexpr uint32_t p16 = 40960;    // P fp16, 64 x 128 B
+constexpr uint32_t tw = 57344;     // [Tw; Tb_hi] (input dtype): one M = 128 operand; later W fp16
+constexpr uint32_t zz = 73728;     // [0; Tb_lo]: one M = 128 operand; later U_hi fp16
+constexpr uint32_t amat = 90112;   // fp32 A / T (64 x kAStride); later o_intra staging
+constexpr uint32_t vec = amat + 17408;  // kVecN x 64 fp32
 constexpr uint32_t bars = vec + kVecN * kC * 4;
 constexpr uint32_t misc = bars + 16 * 8;
 constexpr uint32_t total = misc + 32;
 constexpr uint32_t alloc = total + 1024;
-static_assert(amat + kC * kAStride * 4 <= tw, "A/T overlaps Tw");
-// TMEM columns: S 0-63 (M=128); W 0-127, U 128-255 (M=64); PW 0-127, PU 128-255 (M=64);
-// N 0-127, c 128-255 (M=128).  Packet pieces are staged in shared memory that the
-// finished MMAs no longer read and leave in bulk copies:
-//   Q' in place over q; o_intra over P (slices 0-1) and Tw (slices 2-3);
-//   N over U_hi (block 0) and U_lo (block 1); c over Kbar (slices 0-1) and W (slices 2-3).
+static_assert(kC * kAStride * 4 <= 17408, "A/T region");
+static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
+// TMEM columns: S 0-63 (M=128); [W | Tw V ; Tb K | U] 0-255 (M=128: W = lanes 0-63 cols 0-127,
+// U = lanes 64-127 cols 128-255); PW 0-127, PU 128-255 (M=64); N 0-127, c 128-255 (M=128).
+// Packet pieces are staged in shared memory that the finished MMAs no longer
+// read and leave in bulk copies: Q' in place over q, o_intra over A/T,
+// N over [W | U_hi], c over [Kbar | U_lo].
 enum { B_FULL = 0, B_SFULL, B_TREADY, B_WUFULL, B_EPA, B_PFULL, B_EPC, B_NCFULL, B_DONE, B_COUNT };
 }  // namespace wy
 
@@ -140,12 +143,24 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
   if (warp == 4) {
     if (lane == 0) {
       mbar_arrive_expect_tx(&bars[wy::B_FULL], 49152);
-      tma_load_4d(sm + wy::kq, &P.tm_k, &bars[wy::B_FULL], 0, t0, hh, bb);
-      tma_load_4d(sm + wy::kq + 8192, &P.tm_q, &bars[wy::B_FULL], 0, t0, hh, bb);
-      tma_load_4d(sm + wy::kq + 16384, &P.tm_k, &bars[wy::B_FULL], 64, t0, hh, bb);
-      tma_load_4d(sm + wy::kq + 24576, &P.tm_q, &bars[wy::B_FULL], 64, t0, hh, bb);
-      tma_load_4d(sm + wy::vt, &P.tm_v, &bars[wy::B_FULL], 0, t0, hh, bb);
-      tma_load_4d(sm + wy::vt + 8192, &P.tm_v, &bars[wy::B_FULL], 64, t0, hh, bb);
+      tma_load_4d(sm + wy::k0, &P.tm_k, &bars[wy::B_FULL], 0, t0, hh, bb);
+      tma_load_4d(sm + wy::q0, &P.tm_q, &bars[wy::B_FULL], 0, t0, hh, bb);
+      tma_load_4d(sm + wy::k1, &P.tm_k, &bars[wy::B_FULL], 64, t0, hh, bb);
+      tma_load_4d(sm + wy::q1, &P.tm_q, &bars[wy::B_FULL], 64, t0, hh, bb);
+      tma_load_4d(sm + wy::v0, &P.tm_v, &bars[wy::B_FULL], 0, t0, hh, bb);
+      tma_load_4d(sm + wy::v1, &P.tm_v, &bars[wy::B_FULL], 64, t0, hh, bb);
+      // the CTA that most likely takes this one's place on the SM: its inputs into L2
+      const int nb = blockIdx.x + P.pf_stride;
+      if (P.pf_stride > 0 && nb < int(gridDim.x)) {
+        const int nbh = nb / P.NS, nt0 = (P.c0 + nb % P.NS) * kC;
+        const int nhh = nbh % P.H, nbb = nbh / P.H;
+        tma_prefetch_4d(&P.tm_k, 0, nt0, nhh, nbb);
+        tma_prefetch_4d(&P.tm_k, 64, nt0, nhh, nbb);
+        tma_prefetch_4d(&P.tm_q, 0, nt0, nhh, nbb);
+        tma_prefetch_4d(&P.tm_q, 64, nt0, nhh, nbb);
+        tma_prefetch_4d(&P.tm_v, 0, nt0, nhh, nbb);
+        tma_prefetch_4d(&P.tm_v, 64, nt0, nhh, nbb);
+      }
     }
     // in-chunk cumsum of g (log2 units) and beta; zero past T (gdn_ref.py:102-114)
     constexpr float kLog2e = 1.4426950408889634f;
@@ -188,25 +203,26 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       const uint32_t id_s = idesc_f16(128, 64, kInBf16, 0, 0);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t a = sb + wy::kq + (kk >> 2) * 16384 + (kk & 3) * 32;
+        const uint32_t a = sb + wy::k0 + (kk >> 2) * 16384 + (kk & 3) * 32;
         mma_f16_ss_warp(tmem, sdesc(a, 16, 1024, kSw128), sdesc(a, 16, 1024, kSw128), id_s, kk > 0);
       }
       mma_commit_warp(&bars[wy::B_SFULL]);
       ok = mbar_wait_warp(&bars[wy::B_TREADY], 0, abort_flag);
     }
     if (ok) {
-      // W = Tw K (M=64, N=128, K=64; B = k read MN-major) -> cols 0-127
-      // U = Tb_hi V + Tb_lo V (M=64, N=128, K=64 twice)   -> cols 128-255
+      // [Tw; Tb_hi] [K | V] (M=128, N=256, K=64), then [0; Tb_lo] V into cols 128-255:
+      // W = lanes 0-63 x cols 0-127, U = Tb_hi V + Tb_lo V = lanes 64-127 x cols 128-255
       tc_fence_after();
-      const uint32_t id_w = idesc_f16(64, 128, kInBf16, 0, 1);
+      const uint32_t id_wu = idesc_f16(128, 256, kInBf16, 0, 1);
+      const uint32_t id_lo = idesc_f16(128, 128, kInBf16, 0, 1);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
         mma_f16_ss_warp(tmem, sdesc(sb + wy::tw + kk * 32, 16, 1024, kSw128),
-                        sdesc(sb + wy::kq + kk * 2048, 16384, 1024, kSw128), id_w, kk > 0);
+                        sdesc(sb + wy::k0 + kk * 2048, 16384, 1024, kSw128), id_wu, kk > 0);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::tb + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024, kSw128),
-                        sdesc(sb + wy::vt + (kk & 3) * 2048, 8192, 1024, kSw128), id_w, kk > 0);
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::zz + kk * 32, 16, 1024, kSw128),
+                        sdesc(sb + wy::v0 + kk * 2048, 16384, 1024, kSw128), id_lo, 1);
       mma_commit_warp(&bars[wy::B_WUFULL]);
       ok = mbar_wait_warp(&bars[wy::B_EPA], 0, abort_flag);
     }
@@ -217,12 +233,13 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
         mma_f16_ss_warp(tmem, sdesc(sb + wy::p16 + kk * 32, 16, 1024, kSw128),
-                        sdesc(sb + wy::amat + kk * 2048, 8192, 1024, kSw128), id_p, kk > 0);
+                        sdesc(sb + wy::tw + kk * 2048, 8192, 1024, kSw128), id_p, kk > 0);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
         mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::p16 + (kk & 3) * 32, 16, 1024, kSw128),
-                        sdesc(sb + (kk < 4 ? wy::vt : wy::tb) + (kk & 3) * 2048, 8192, 1024, kSw128), id_p,
-                        kk > 0);
+                        kk < 4 ? sdesc(sb + wy::zz + (kk & 3) * 2048, 8192, 1024, kSw128)
+                               : sdesc(sb + wy::v0 + (kk & 3) * 2048, 16384, 1024, kSw128),
+                        id_p, kk > 0);
       mma_commit_warp(&bars[wy::B_PFULL]);
       ok = mbar_wait_warp(&bars[wy::B_EPC], 0, abort_flag);
     }
@@ -232,13 +249,14 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       const uint32_t id_n = idesc_f16(128, 128, 0, 1, 1);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss_warp(tmem, sdesc(sb + wy::kq + kk * 2048, 16384, 1024, kSw128),
-                        sdesc(sb + wy::amat + kk * 2048, 8192, 1024, kSw128), id_n, kk > 0);
+        mma_f16_ss_warp(tmem, sdesc(sb + wy::k0 + kk * 2048, 16384, 1024, kSw128),
+                        sdesc(sb + wy::tw + kk * 2048, 8192, 1024, kSw128), id_n, kk > 0);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::kq + (kk & 3) * 2048, 16384, 1024, kSw128),
-                        sdesc(sb + (kk < 4 ? wy::vt : wy::tb) + (kk & 3) * 2048, 8192, 1024, kSw128), id_n,
-                        kk > 0);
+        mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::k0 + (kk & 3) * 2048, 16384, 1024, kSw128),
+                        kk < 4 ? sdesc(sb + wy::zz + (kk & 3) * 2048, 8192, 1024, kSw128)
+                               : sdesc(sb + wy::v0 + (kk & 3) * 2048, 16384, 1024, kSw128),
+                        id_n, kk > 0);
       mma_commit_warp(&bars[wy::B_NCFULL]);
     }
     if (!ok && lane == 0) *abort_flag = 1;
@@ -295,8 +313,12 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         const int r = ptid >> 1, half = ptid & 1;
         const float* trow = amat + r * kAStride;
         uint8_t* twp = sm + wy::tw;
-        uint8_t* hip = sm + wy::tb;
-        uint8_t* lop = sm + wy::tb + 8192;
+        uint8_t* hip = sm + wy::tw + 8192;
+        uint8_t* lop = sm + wy::zz + 8192;
+        // the zero upper half of [0; Tb_lo]
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(sm + wy::zz + ptid * 64 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll 1
         for (int c = 4 * half; c < 4 * half + 4; ++c) {
           uint32_t ww[4], hi[4], lo[4];
@@ -319,63 +341,56 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       if (lane == 0) mbar_arrive(&bars[wy::B_TREADY]);
       if (ptid == 0) WY_TR(5);
     }
-    // ---- epilogue A: W -> fp16 [t][k] (over A/T), U -> fp16 hi (over v) + lo (over Tb),
-    //      k -> Kbar = e^{b_C - b_t} k fp16 in place.  W and U are M=64 accumulators:
-    //      row 16w + l lives in TMEM lane 32w + l (l < 16).
+    // ---- epilogue A: lanes 0-63 W -> fp16 [t][k] (over [Tw; Tb_hi]); lanes 64-127 U -> fp16
+    //      hi (over [0; Tb_lo]) and lo (over v); every lane: half a row of k -> Kbar fp16 in place
     ok = ok && mbar_wait_warp(&bars[wy::B_WUFULL], 0, abort_flag);
     if (ptid == 0) WY_TR(6);
     if (ok) {
       tc_fence_after();
-      const int t = 16 * warp + (lane & 15);
+      const int t = ptid & 63;
+      const bool isw = ptid < 64;
 #pragma unroll 1
       for (int c0 = 0; c0 < 128; c0 += 32) {
-        float w[32];
-        tmem_ld32w(tmem_addr(tmem, warp * 32, c0), w);
-        if (lane < 16) {
-          uint8_t* dst = sm + wy::amat + (c0 >> 6) * 8192;
+        float x[32];
+        tmem_ld32w(tmem_addr(tmem, warp * 32, (isw ? 0 : 128) + c0), x);
+        const uint32_t chunk0 = (c0 & 63) >> 3;
+        if (isw) {
+          uint8_t* dst = sm + wy::tw + (c0 >> 6) * 8192;
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(dst + sw128_off(t, ((c0 & 63) >> 3) + c)) = pack8_f16(w + 8 * c);
-        }
-      }
-#pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
-        float u[32];
-        tmem_ld32w(tmem_addr(tmem, warp * 32, 128 + c0), u);
-        if (lane < 16) {
-          uint8_t* dhi = sm + wy::vt + (c0 >> 6) * 8192;
-          uint8_t* dlo = sm + wy::tb + (c0 >> 6) * 8192;
+            *reinterpret_cast<uint4*>(dst + sw128_off(t, chunk0 + c)) = pack8_f16(x + 8 * c);
+        } else {
+          uint8_t* dhi = sm + wy::zz + (c0 >> 6) * 8192;
+          uint8_t* dlo = sm + wy::v0 + (c0 >> 6) * 16384;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             float hi[8], lo[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              hi[e] = __half2float(__float2half_rn(u[8 * c + e]));
-              lo[e] = u[8 * c + e] - hi[e];
+              hi[e] = __half2float(__float2half_rn(x[8 * c + e]));
+              lo[e] = x[8 * c + e] - hi[e];
             }
-            const uint32_t off = sw128_off(t, ((c0 & 63) >> 3) + c);
+            const uint32_t off = sw128_off(t, chunk0 + c);
             *reinterpret_cast<uint4*>(dhi + off) = pack8_f16(hi);
             *reinterpret_cast<uint4*>(dlo + off) = pack8_f16(lo);
           }
         }
       }
-      if (lane >= 16) {
+      {
         const float dd = vec[V_DD * kC + t];
-#pragma unroll 1
-        for (int cb = 0; cb < 2; ++cb) {
+        uint8_t* kb = sm + (isw ? wy::k0 : wy::k1);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4* p = reinterpret_cast<uint4*>(sm + wy::kq + cb * 16384 + sw128_off(t, c));
-            const uint4 x = *p;
-            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-            uint32_t ys[4];
+        for (int c = 0; c < 8; ++c) {
+          uint4* p = reinterpret_cast<uint4*>(kb + sw128_off(t, c));
+          const uint4 x = *p;
+          const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+          uint32_t ys[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = Cvt<InT>::unpack(xs[e]);
-              ys[e] = Cvt<__half>::pack(f.x * dd, f.y * dd);
-            }
-            *p = make_uint4(ys[0], ys[1], ys[2], ys[3]);
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = Cvt<InT>::unpack(xs[e]);
+            ys[e] = Cvt<__half>::pack(f.x * dd, f.y * dd);
           }
+          *p = make_uint4(ys[0], ys[1], ys[2], ys[3]);
         }
       }
       fence_async_smem();
@@ -397,7 +412,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         float pw[32];
         tmem_ld32w(tmem_addr(tmem, warp * 32, c0), pw);
         if (lane < 16) {
-          uint8_t* qrow = sm + wy::kq + 8192 + (c0 >> 6) * 16384;
+          uint8_t* qrow = sm + wy::q0 + (c0 >> 6) * 16384;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint4* p = reinterpret_cast<uint4*>(qrow + sw128_off(t, ((c0 & 63) >> 3) + c));
@@ -419,8 +434,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         float ou[32];
         tmem_ld32w(tmem_addr(tmem, warp * 32, 128 + c0), ou);
         if (lane < 16) {
-          const int sl = c0 >> 5;
-          uint8_t* dst = sm + (sl < 2 ? wy::p16 : wy::tw) + (sl & 1) * 4096;
+          uint8_t* dst = sm + wy::amat + (c0 >> 5) * 4096;
 #pragma unroll
           for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + sw64_off(t, c)) = pack8_f16(ou + 8 * c);
         }
@@ -431,10 +445,9 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       fence_async_smem();
       named_bar(1, 128);
       if (ptid == 0) {
-        bulk_store(pkg + pkt::kQ, sm + wy::kq + 8192, 8192);
-        bulk_store(pkg + pkt::kQ + 8192, sm + wy::kq + 24576, 8192);
-        bulk_store(pkg + pkt::kOs, sm + wy::p16, 8192);
-        bulk_store(pkg + pkt::kOs + 8192, sm + wy::tw, 8192);
+        bulk_store(pkg + pkt::kQ, sm + wy::q0, 8192);
+        bulk_store(pkg + pkt::kQ + 8192, sm + wy::q1, 8192);
+        bulk_store(pkg + pkt::kOs, sm + wy::amat, 16384);
         bulk_commit();
         WY_TR(11);
       }
@@ -452,7 +465,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         tmem_ld32w(tmem_addr(tmem, warp * 32, c0), n);
 #pragma unroll
         for (int e = 0; e < 32; ++e) n[e] = -n[e];
-        uint8_t* dst = sm + (c0 < 64 ? wy::vt : wy::tb);
+        uint8_t* dst = sm + (c0 < 64 ? wy::tw : wy::zz);
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           *reinterpret_cast<uint4*>(dst + sw128_off(r, ((c0 & 63) >> 3) + c)) = pack8_f16(n + 8 * c);
@@ -461,8 +474,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       for (int c0 = 0; c0 < 128; c0 += 32) {
         float cv[32];
         tmem_ld32w(tmem_addr(tmem, warp * 32, 128 + c0), cv);
-        const int sl = c0 >> 5;
-        uint8_t* dst = sm + (sl < 2 ? wy::kq + sl * 16384 : wy::amat + (sl & 1) * 8192);
+        uint8_t* dst = sm + wy::k0 + (c0 >> 5) * 16384;  // k0, k1, v0 (= U_lo 0), v1
 #pragma unroll
         for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + sw64_off(r, c)) = pack8_f16(cv + 8 * c);
       }
@@ -471,12 +483,12 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       fence_async_smem();
       named_bar(1, 128);
       if (ptid == 0) {
-        bulk_store(pkg + pkt::kN, sm + wy::vt, 16384);
-        bulk_store(pkg + pkt::kN + 16384, sm + wy::tb, 16384);
-        bulk_store(pkg + pkt::kCs, sm + wy::kq, 8192);
-        bulk_store(pkg + pkt::kCs + 8192, sm + wy::kq + 16384, 8192);
-        bulk_store(pkg + pkt::kCs + 16384, sm + wy::amat, 8192);
-        bulk_store(pkg + pkt::kCs + 24576, sm + wy::amat + 8192, 8192);
+        bulk_store(pkg + pkt::kN, sm + wy::tw, 16384);
+        bulk_store(pkg + pkt::kN + 16384, sm + wy::zz, 16384);
+        bulk_store(pkg + pkt::kCs, sm + wy::k0, 8192);
+        bulk_store(pkg + pkt::kCs + 8192, sm + wy::k1, 8192);
+        bulk_store(pkg + pkt::kCs + 16384, sm + wy::v0, 8192);
+        bulk_store(pkg + pkt::kCs + 24576, sm + wy::v1, 8192);
         bulk_commit();
         WY_TR(9);
       }

@@ -18,6 +18,7 @@ struct WyParams {
   long long sb_b, sb_t, sb_h;
   long long sg_b, sg_t, sg_h;
   int B, T, H, c0, NS;  // segment = chunks [c0, c0 + NS)
+  int pf_stride;        // CTAs resident at once (2 per SM): blockIdx + pf_stride is prefetched to L2
 };
 
 // Serial scan over the packets of one segment.
