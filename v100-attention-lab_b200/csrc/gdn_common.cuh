@@ -86,7 +86,7 @@ __device__ __forceinline__ void st_row16(uint8_t* tile, uint32_t r, uint32_t c16
 
 // ------------------------------------------------------------------ the inverse
 // T = (I + A)^-1 for the 64x64 strictly-lower A held in `am` (row stride
-// kAStride), in place, by the 128 prep threads (named barrier 1).  Eight 8x8
+// kAStride), in place, by NTH = 128 or 256 threads (named barrier 1).  Eight 8x8
 // diagonal blocks are inverted by column forward substitution; three
 // doubling levels (8 -> 16 -> 32 -> 64) then apply
 //     inv([[L0, 0], [X, L1]]) = [[inv(L0), 0], [-inv(L1) X inv(L0), inv(L1)]].
@@ -97,31 +97,45 @@ __device__ __forceinline__ void st_row16(uint8_t* tile, uint32_t r, uint32_t c16
 // Phase 1 sums over m >= 4q only (inv(L0) is lower triangular), phase 2 over
 // p <= i only (inv(L1) likewise); items are paired (q with N/4-1-q, i with
 // N-1-i) so that every lane of a warp runs the same number of iterations.
-template <int N>
+template <int N, int NTH>
 struct InvItems {
   static constexpr int NB = 64 / (2 * N), NQ = N / 4;
-  static constexpr int PER = (NB * N * NQ + 127) / 128;  // items per thread (1 or 2)
+  static constexpr int PER = (NB * N * NQ + NTH - 1) / NTH;  // items per thread (1 or 2)
   __device__ static bool p1(int tid, int e, int& blk, int& i, int& q) {
     if constexpr (N == 32) {
-      blk = 0; i = tid & 31; q = e == 0 ? (tid >> 5) : NQ - 1 - (tid >> 5);
+      blk = 0;
+      i = tid & 31;
+      if constexpr (NTH == 256) {
+        const int w = tid >> 5;  // warps w and w + 4 share a sub-partition: q and 7 - q
+        q = w < 4 ? w : 11 - w;
+      } else {
+        q = e == 0 ? (tid >> 5) : NQ - 1 - (tid >> 5);
+      }
       return true;
     } else if constexpr (N == 16) {
-      blk = tid >> 6; i = tid & 15; q = (tid >> 4) & 3;
-      return true;
+      blk = (tid >> 6) & 1; i = tid & 15; q = (tid >> 4) & 3;
+      return tid < 128;
     } else {
-      blk = tid >> 4; i = tid & 7; q = (tid >> 3) & 1;
+      blk = (tid >> 4) & 3; i = tid & 7; q = (tid >> 3) & 1;
       return tid < 64;
     }
   }
   __device__ static bool p2(int tid, int e, int& blk, int& i, int& q) {
     if constexpr (N == 32) {
-      blk = 0; q = tid & 7; i = e == 0 ? (tid >> 3) : N - 1 - (tid >> 3);
+      blk = 0;
+      q = tid & 7;
+      if constexpr (NTH == 256) {
+        const int w = tid >> 5, g = w < 4 ? w : 11 - w;  // row groups g and 7 - g per sub-partition
+        i = 4 * g + ((tid & 31) >> 3);
+      } else {
+        i = e == 0 ? (tid >> 3) : N - 1 - (tid >> 3);
+      }
       return true;
     } else if constexpr (N == 16) {
-      blk = tid >> 6; q = tid & 3; i = (tid >> 2) & 15;
-      return true;
+      blk = (tid >> 6) & 1; q = tid & 3; i = (tid >> 2) & 15;
+      return tid < 128;
     } else {
-      blk = tid >> 4; q = tid & 1; i = (tid >> 1) & 7;
+      blk = (tid >> 4) & 3; q = tid & 1; i = (tid >> 1) & 7;
       return tid < 64;
     }
   }
@@ -134,9 +148,9 @@ __device__ __forceinline__ void fma4(float4& acc, float a, const float4& b) {
   acc.w = fmaf(a, b.w, acc.w);
 }
 
-template <int N>
+template <int N, int NTH>
 __device__ __forceinline__ void inv_level(float* am, int tid) {
-  using It = InvItems<N>;
+  using It = InvItems<N, NTH>;
   constexpr int S = kAStride;
   float4 acc[It::PER];
   // phase 1: Y = X inv(L0); X = rows N..2N-1 x cols 0..N-1 of each 2N block
@@ -161,7 +175,7 @@ __device__ __forceinline__ void inv_level(float* am, int tid) {
     }
     acc[e] = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
   }
-  named_bar(1, 128);
+  named_bar(1, NTH);
 #pragma unroll
   for (int e = 0; e < It::PER; ++e) {
     int blk, i, q;
@@ -170,7 +184,7 @@ __device__ __forceinline__ void inv_level(float* am, int tid) {
       *reinterpret_cast<float4*>(am + (o + N + i) * S + o + 4 * q) = acc[e];
     }
   }
-  named_bar(1, 128);
+  named_bar(1, NTH);
   // phase 2: T = -inv(L1) Y
 #pragma unroll
   for (int e = 0; e < It::PER; ++e) {
@@ -193,7 +207,7 @@ __device__ __forceinline__ void inv_level(float* am, int tid) {
     }
     acc[e] = make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
   }
-  named_bar(1, 128);
+  named_bar(1, NTH);
 #pragma unroll
   for (int e = 0; e < It::PER; ++e) {
     int blk, i, q;
@@ -203,9 +217,10 @@ __device__ __forceinline__ void inv_level(float* am, int tid) {
           make_float4(-acc[e].x, -acc[e].y, -acc[e].z, -acc[e].w);
     }
   }
-  named_bar(1, 128);
+  named_bar(1, NTH);
 }
 
+template <int NTH = 128>
 __device__ __forceinline__ void invert_unit_lower64(float* am, int ptid) {
   if (ptid < 64) {
     const int blk_id = ptid >> 3, c = ptid & 7;
@@ -229,10 +244,10 @@ __device__ __forceinline__ void invert_unit_lower64(float* am, int ptid) {
 #pragma unroll
     for (int t = 0; t < 8; ++t) blk[t * kAStride + c] = x[t];
   }
-  named_bar(1, 128);
-  inv_level<8>(am, ptid);
-  inv_level<16>(am, ptid);
-  inv_level<32>(am, ptid);
+  named_bar(1, NTH);
+  inv_level<8, NTH>(am, ptid);
+  inv_level<16, NTH>(am, ptid);
+  inv_level<32, NTH>(am, ptid);
 }
 
 }  // namespace gdn

@@ -51,7 +51,11 @@ static_assert(kOs + 4 * 4096 == kPacketBytesPerChunk, "packet size");
 
 // =========================================================== prep kernel
 namespace wy {
-constexpr int kThreads = 160;      // warps 0-3: prep (TMEM lanes 0-127), warp 4: TMA + MMA
+// warps 0-7: prep (warp w reads TMEM lane quarter w & 3 and takes column half w >> 2);
+// warp 8: TMA + MMA
+constexpr int kThreads = 288;
+constexpr int kPrep = 256;
+constexpr int kMmaWarp = 8;
 // Column blocks of 64 elements (128-byte rows, 128B swizzle).  k0, k1, v0, v1
 // sit 16 KB apart so that [K | V] is one N = 256 MN-major operand.
 constexpr uint32_t k0 = 0, q0 = 8192, k1 = 16384, q1 = 24576;  // k later -> Kbar fp16 in place
@@ -116,11 +120,11 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
 
   if (tid == 0) {
     for (int i = 0; i < wy::B_COUNT; ++i)
-      mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC) ? 4 : 1);
+      mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC) ? wy::kPrep / 32 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == wy::kMmaWarp) {
     tmem_alloc(tmem_base_p, 256);
     tmem_relinquish();
   }
@@ -140,7 +144,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
 #endif
   if (tid == 0) WY_TR(0);
 
-  if (warp == 4) {
+  if (warp == wy::kMmaWarp) {
     if (lane == 0) {
       mbar_arrive_expect_tx(&bars[wy::B_FULL], 49152);
       tma_load_4d(sm + wy::k0, &P.tm_k, &bars[wy::B_FULL], 0, t0, hh, bb);
@@ -193,7 +197,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
 
   constexpr uint32_t kInBf16 = Cvt<InT>::kIsBf16;
   bool ok = true;
-  if (warp == 4) {
+  if (warp == wy::kMmaWarp) {
     // ------------------------------------------------ MMA issue (the whole warp; elect.sync inside)
     ok = mbar_wait_warp(&bars[wy::B_FULL], 0, abort_flag);
     if (lane == 0) WY_TR(1);
@@ -262,39 +266,42 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     if (!ok && lane == 0) *abort_flag = 1;
     __syncwarp();
   } else {
-    // ------------------------------------------------ prep (warps 0-3, thread = TMEM lane)
-    const int ptid = tid;
+    // ------------------------------------------------ prep (warps 0-7)
+    constexpr int NP = wy::kPrep;
+    const int ptid = tid;                     // 0..255
+    const int lq = warp & 3, hc = warp >> 2;  // TMEM lane quarter, column half
+    const int r = (lq << 5) | lane;           // TMEM lane = row of an M=128 accumulator
     const float b2first = vec[V_B2 * kC], b2last = vec[V_B2 * kC + kC - 1];
     const float ref = 0.5f * (b2first + b2last);
     const bool prod_form = (b2first - b2last) < 200.f;
     if (ptid < 64) amat[ptid * kAStride + 64] = fast_exp2(ref - vec[V_B2 * kC + ptid]);
-    named_bar(2, 128);
+    named_bar(2, NP);
     ok = mbar_wait_warp(&bars[wy::B_SFULL], 0, abort_flag);
     if (ptid == 0) WY_TR(2);
-    if (bar_any(1, 128, !ok || *abort_flag)) ok = false;
+    if (bar_any(1, NP, !ok || *abort_flag)) ok = false;
     if (ok) {
       tc_fence_after();
       // rows 0-63: A[t][m] = beta_t exp(b_t - b_m) (k_t.k_m), m < t   (TMEM lanes 0-63 = K K^T)
       // rows 64-127: P[t][m] = exp(b_t - b_m) (q_t.k_m), m <= t      (lanes 64-127 = Q K^T)
-      const int t = ptid & 63;
+      const int t = r & 63;
       const float b2t = vec[V_B2 * kC + t];
       const float et = fast_exp2(b2t - ref);
-      const float bt = (ptid < 64) ? vec[V_BETA * kC + t] : 1.f;
+      const float bt = (r < 64) ? vec[V_BETA * kC + t] : 1.f;
       float* arow = amat + t * kAStride;
       uint8_t* pimg = sm + wy::p16;
 #pragma unroll 1
-      for (int cg = 0; cg < 4; ++cg) {
-        float s[16];
-        tmem_ld16w(tmem_addr(tmem, warp * 32, cg * 16), s);
+      for (int cg = 2 * hc; cg < 2 * hc + 2; ++cg) {
+        float sv[16];
+        tmem_ld16w(tmem_addr(tmem, lq * 32, cg * 16), sv);
         float x[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int m = cg * 16 + e;
           const float dec = prod_form ? et * amat[m * kAStride + 64] : fast_exp2(b2t - vec[V_B2 * kC + m]);
-          const bool keep = (ptid < 64) ? (m < t) : (m <= t);
-          x[e] = keep ? bt * dec * s[e] : 0.f;
+          const bool keep = (r < 64) ? (m < t) : (m <= t);
+          x[e] = keep ? bt * dec * sv[e] : 0.f;
         }
-        if (ptid < 64) {
+        if (r < 64) {
 #pragma unroll
           for (int e = 0; e < 16; e += 4)
             *reinterpret_cast<float4*>(arow + cg * 16 + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
@@ -304,23 +311,19 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         }
       }
       tc_fence_before();
-      named_bar(1, 128);
+      named_bar(1, NP);
       if (ptid == 0) WY_TR(3);
-      invert_unit_lower64(amat, ptid);  // T = (I + A)^-1 in place
+      invert_unit_lower64<NP>(amat, ptid);  // T = (I + A)^-1 in place
       if (ptid == 0) WY_TR(4);
-      // Tw = T diag(beta e^b) -> tw; Tb = T diag(beta) -> hi + lo (input dtype, MMA operands)
+      // Tw = T diag(beta e^b) -> [Tw; .]; Tb = T diag(beta) -> hi [.; Tb_hi] + lo [0; Tb_lo]
       {
-        const int r = ptid >> 1, half = ptid & 1;
-        const float* trow = amat + r * kAStride;
+        const int rr = ptid >> 2, cq = ptid & 3;
+        const float* trow = amat + rr * kAStride;
         uint8_t* twp = sm + wy::tw;
         uint8_t* hip = sm + wy::tw + 8192;
         uint8_t* lop = sm + wy::zz + 8192;
-        // the zero upper half of [0; Tb_lo]
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(sm + wy::zz + ptid * 64 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll 1
-        for (int c = 4 * half; c < 4 * half + 4; ++c) {
+        for (int c = 2 * cq; c < 2 * cq + 2; ++c) {
           uint32_t ww[4], hi[4], lo[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -331,28 +334,31 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
             const float2 hf = Cvt<InT>::unpack(hi[e]);
             lo[e] = Cvt<InT>::pack(tb0 - hf.x, tb1 - hf.y);
           }
-          *reinterpret_cast<uint4*>(twp + sw128_off(r, c)) = make_uint4(ww[0], ww[1], ww[2], ww[3]);
-          *reinterpret_cast<uint4*>(hip + sw128_off(r, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-          *reinterpret_cast<uint4*>(lop + sw128_off(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          *reinterpret_cast<uint4*>(twp + sw128_off(rr, c)) = make_uint4(ww[0], ww[1], ww[2], ww[3]);
+          *reinterpret_cast<uint4*>(hip + sw128_off(rr, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(lop + sw128_off(rr, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
+        // the zero upper half of [0; Tb_lo]
+        *reinterpret_cast<uint4*>(sm + wy::zz + ptid * 32) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(sm + wy::zz + ptid * 32 + 16) = make_uint4(0u, 0u, 0u, 0u);
       }
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[wy::B_TREADY]);
       if (ptid == 0) WY_TR(5);
     }
-    // ---- epilogue A: lanes 0-63 W -> fp16 [t][k] (over [Tw; Tb_hi]); lanes 64-127 U -> fp16
-    //      hi (over [0; Tb_lo]) and lo (over v); every lane: half a row of k -> Kbar fp16 in place
+    // ---- epilogue A: rows 0-63 W -> fp16 [t][k] (over [Tw; Tb_hi]); rows 64-127 U -> fp16
+    //      hi (over [0; Tb_lo]) and lo (over v); and k -> Kbar = e^{b_C - b_t} k fp16 in place
     ok = ok && mbar_wait_warp(&bars[wy::B_WUFULL], 0, abort_flag);
     if (ptid == 0) WY_TR(6);
     if (ok) {
       tc_fence_after();
-      const int t = ptid & 63;
-      const bool isw = ptid < 64;
+      const int t = r & 63;
+      const bool isw = r < 64;
 #pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
+      for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
         float x[32];
-        tmem_ld32w(tmem_addr(tmem, warp * 32, (isw ? 0 : 128) + c0), x);
+        tmem_ld32w(tmem_addr(tmem, lq * 32, (isw ? 0 : 128) + c0), x);
         const uint32_t chunk0 = (c0 & 63) >> 3;
         if (isw) {
           uint8_t* dst = sm + wy::tw + (c0 >> 6) * 8192;
@@ -380,9 +386,9 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         const float dd = vec[V_DD * kC + t];
         uint8_t* kb = sm + (isw ? wy::k0 : wy::k1);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4* p = reinterpret_cast<uint4*>(kb + sw128_off(t, c));
-          const uint4 x = *p;
+        for (int c = 4 * hc; c < 4 * hc + 4; ++c) {
+          uint4* pp = reinterpret_cast<uint4*>(kb + sw128_off(t, c));
+          const uint4 x = *pp;
           const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
           uint32_t ys[4];
 #pragma unroll
@@ -390,7 +396,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
             const float2 f = Cvt<InT>::unpack(xs[e]);
             ys[e] = Cvt<__half>::pack(f.x * dd, f.y * dd);
           }
-          *p = make_uint4(ys[0], ys[1], ys[2], ys[3]);
+          *pp = make_uint4(ys[0], ys[1], ys[2], ys[3]);
         }
       }
       fence_async_smem();
@@ -399,24 +405,25 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       if (lane == 0) mbar_arrive(&bars[wy::B_EPA]);
       if (ptid == 0) WY_TR(7);
     }
-    // ---- epilogue C: Q' = e^{b_t} q_t - (P W)_t (in place over q) and o_intra = P U (M=64 rows)
+    // ---- epilogue C: Q' = e^{b_t} q_t - (P W)_t (in place over q) and o_intra = P U (M=64:
+    //      row 16 lq + l in lane 32 lq + l, l < 16)
     ok = ok && mbar_wait_warp(&bars[wy::B_PFULL], 0, abort_flag);
     if (ptid == 0) WY_TR(10);
-    if (bar_any(1, 128, !ok || *abort_flag)) ok = false;  // uniform: named barriers follow
+    if (bar_any(1, NP, !ok || *abort_flag)) ok = false;  // uniform: named barriers follow
     if (ok) {
       tc_fence_after();
-      const int t = 16 * warp + (lane & 15);
+      const int t = 16 * lq + (lane & 15);
       const float eb = vec[V_EB * kC + t];
 #pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
+      for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
         float pw[32];
-        tmem_ld32w(tmem_addr(tmem, warp * 32, c0), pw);
+        tmem_ld32w(tmem_addr(tmem, lq * 32, c0), pw);
         if (lane < 16) {
           uint8_t* qrow = sm + wy::q0 + (c0 >> 6) * 16384;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            uint4* p = reinterpret_cast<uint4*>(qrow + sw128_off(t, ((c0 & 63) >> 3) + c));
-            const uint4 x = *p;
+            uint4* pp = reinterpret_cast<uint4*>(qrow + sw128_off(t, ((c0 & 63) >> 3) + c));
+            const uint4 x = *pp;
             const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
             float y[8];
 #pragma unroll
@@ -425,14 +432,14 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
               y[2 * e] = fmaf(eb, f.x, -pw[8 * c + 2 * e]);
               y[2 * e + 1] = fmaf(eb, f.y, -pw[8 * c + 2 * e + 1]);
             }
-            *p = pack8_f16(y);
+            *pp = pack8_f16(y);
           }
         }
       }
 #pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
+      for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
         float ou[32];
-        tmem_ld32w(tmem_addr(tmem, warp * 32, 128 + c0), ou);
+        tmem_ld32w(tmem_addr(tmem, lq * 32, 128 + c0), ou);
         if (lane < 16) {
           uint8_t* dst = sm + wy::amat + (c0 >> 5) * 4096;
 #pragma unroll
@@ -443,7 +450,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[wy::B_EPC]);
       fence_async_smem();
-      named_bar(1, 128);
+      named_bar(1, NP);
       if (ptid == 0) {
         bulk_store(pkg + pkt::kQ, sm + wy::q0, 8192);
         bulk_store(pkg + pkt::kQ + 8192, sm + wy::q1, 8192);
@@ -455,14 +462,13 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     // ---- epilogue B: N = -(Kbar^T W) and c = Kbar^T U (row k1 = TMEM lane)
     ok = ok && mbar_wait_warp(&bars[wy::B_NCFULL], 0, abort_flag);
     if (ptid == 0) WY_TR(8);
-    if (bar_any(1, 128, !ok || *abort_flag)) ok = false;
+    if (bar_any(1, NP, !ok || *abort_flag)) ok = false;
     if (ok) {
       tc_fence_after();
-      const int r = ptid;
 #pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
+      for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
         float n[32];
-        tmem_ld32w(tmem_addr(tmem, warp * 32, c0), n);
+        tmem_ld32w(tmem_addr(tmem, lq * 32, c0), n);
 #pragma unroll
         for (int e = 0; e < 32; ++e) n[e] = -n[e];
         uint8_t* dst = sm + (c0 < 64 ? wy::tw : wy::zz);
@@ -471,17 +477,17 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
           *reinterpret_cast<uint4*>(dst + sw128_off(r, ((c0 & 63) >> 3) + c)) = pack8_f16(n + 8 * c);
       }
 #pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
+      for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
         float cv[32];
-        tmem_ld32w(tmem_addr(tmem, warp * 32, 128 + c0), cv);
+        tmem_ld32w(tmem_addr(tmem, lq * 32, 128 + c0), cv);
         uint8_t* dst = sm + wy::k0 + (c0 >> 5) * 16384;  // k0, k1, v0 (= U_lo 0), v1
 #pragma unroll
         for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + sw64_off(r, c)) = pack8_f16(cv + 8 * c);
       }
-      if (r == 0) *reinterpret_cast<float*>(pkg + pkt::kHdr) = vec[V_EB * kC + kC - 1];
+      if (ptid == 0) *reinterpret_cast<float*>(pkg + pkt::kHdr) = vec[V_EB * kC + kC - 1];
       tc_fence_before();
       fence_async_smem();
-      named_bar(1, 128);
+      named_bar(1, NP);
       if (ptid == 0) {
         bulk_store(pkg + pkt::kN, sm + wy::tw, 16384);
         bulk_store(pkg + pkt::kN + 16384, sm + wy::zz, 16384);
@@ -498,7 +504,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     if (!ok) *abort_flag = 1;
   }
   __syncthreads();
-  if (warp == 4) {
+  if (warp == wy::kMmaWarp) {
     if (lane == 0 && *abort_flag) {
       // a failed wait: let the TMA loads land before the CTA releases its smem
       volatile int never = 0;
