@@ -11,8 +11,11 @@ on BASELINE config 2 (B=2, T=4096, H=16, K=V=128, bf16, C=64, h0 ~ N(0, 0.1)).
 * ``e2e``       the same metric through the public Python API with pinned host
                 buffers: every step copies its inputs host->device and reads o
                 and the final state back.
-* ``roofline``  the kernel's algorithmic bytes per launch / its average
-                duration, against the measured HBM copy bandwidth.
+* ``roofline``  one forward (the prep kernel and the scan kernel it feeds):
+                its algorithmic bytes / its average device time (CUDA events
+                over the timed region), against the measured HBM copy
+                bandwidth; ``traffic`` is the DRAM bytes of both kernels per
+                forward from the committed ncu summary.
 * ``cpu_baseline`` the CPU oracle (numpy port of gdn_ref's chunked path) on the
                 host cores, rank 0 at N=1 only.
 
@@ -255,6 +258,19 @@ def run_reference(args, cfg, rank, world):
     return line
 
 
+def launches_per_forward(B, T, H):
+    """Kernel launches of one gdn_chunk_fwd call: a prep and a scan launch per
+    segment of chunks that fits the (capped) workspace."""
+    from gdn_b200 import _lib, ops
+    nt = -(-T // CHUNK)
+    state = B * H * K_DIM * V_DIM * 4
+    per_chunk = B * H * _lib.PACKET_BYTES_PER_CHUNK
+    need = nt * per_chunk + state
+    ws = max(min(need, ops.WORKSPACE_CAP_BYTES), per_chunk + state)
+    ns_max = (ws - state) // per_chunk
+    return 2 * -(-nt // ns_max)
+
+
 def run_ours(args, cfg, rank, world, local):
     import gdn_b200
     from gdn_b200 import _lib
@@ -368,9 +384,10 @@ def run_ours(args, cfg, rank, world, local):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": measured_traffic(args.config) if world == 1 else None,
                      "peak_source": peak_src, "algorithmic_bytes_per_launch": abytes,
+                     "launch": "one forward = prep kernel + scan kernel",
                      "tensor_frac": flops / kern_s / 1e12 / tf},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": steps,
+        "gpu_launches": steps * launches_per_forward(B_rank, T, H),
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:

@@ -37,7 +37,7 @@ _workspaces: dict[int, torch.Tensor] = {}
 
 # Upper bound of the per-device scratch of the two-kernel path; longer inputs
 # run in several segments of chunks, so memory does not grow with T.
-WORKSPACE_CAP_BYTES = int(os.environ.get("GDN_B200_WORKSPACE_MB", "256")) << 20
+WORKSPACE_CAP_BYTES = int(os.environ.get("GDN_B200_WORKSPACE_MB", "1024")) << 20
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
