@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define GDN_B200_ABI_VERSION 2
+#define GDN_B200_ABI_VERSION 3
 
 /* Element types (q/k/v inputs, o output). */
 enum gdn_dtype {
@@ -46,12 +46,27 @@ enum gdn_status {
 };
 
 /*
+ * Input preparation done inside the kernel (gdn_fwd_args.flags), replacing
+ * the caller-side steps of bench_gdn.py:33-40 / gdn_ref.py:24-25:
+ *   GDN_FLAG_QK_L2NORM     q and k are raw: every row is divided by
+ *                          sqrt(sum of squares + 1e-6) in fp32 before use
+ *   GDN_FLAG_BETA_SIGMOID  beta holds logits: beta = sigmoid(beta)
+ *   GDN_FLAG_G_LOGSIGMOID  g holds logits: g = logsigmoid(g)
+ * Only the two-kernel path (a workspace is given) applies GDN_FLAG_QK_L2NORM;
+ * the fused kernel returns GDN_ERR_UNSUPPORTED for it.
+ */
+#define GDN_FLAG_QK_L2NORM 1
+#define GDN_FLAG_BETA_SIGMOID 2
+#define GDN_FLAG_G_LOGSIGMOID 4
+
+/*
  * Arguments of one forward call.  Shapes follow the reference
  * (gdn_triton.py:116-117, gdn_ref.py:11-14):
  *   q, k  [B, T, H, K]   in_dtype     (last dim contiguous)
  *   v     [B, T, H, V]   in_dtype     (last dim contiguous)
  *   beta  [B, T, H]      float32
- *   g     [B, T, H]      float32      (log decay, <= 0)
+ *   g     [B, T, H]      float32      (log decay, <= 0), or NULL for g == 0
+ *                                    (no decay: the DeltaNet recurrence)
  *   h0    [B, H, V, K]   float32      contiguous, or NULL for a zero state
  *   o     [B, T, H, V]   out_dtype    (last dim contiguous)
  *   ht    [B, H, V, K]   float32      contiguous, or NULL to skip the store
@@ -86,6 +101,10 @@ typedef struct gdn_fwd_args {
    * too small for one chunk per (b, h): the single fused kernel runs instead. */
   void* workspace;
   uint64_t workspace_bytes;
+  /* o is computed with q scaled by `scale` (the FLA convention); 0 means 1,
+   * the reference's behaviour (gdn_ref.py:45 reads q unscaled). */
+  float scale;
+  int32_t flags; /* GDN_FLAG_* */
 } gdn_fwd_args;
 
 /*
@@ -96,7 +115,7 @@ typedef struct gdn_fwd_args {
  * reference allocates them inside its wrapper (gdn_triton.py:126-127).
  *
  * With a workspace it runs two kernels per segment of chunks: the
- * chunk-parallel WY/UT preparation (40 KB of operands per (b, h, chunk) in the
+ * chunk-parallel WY/UT preparation (96.25 KB of operands per (b, h, chunk) in the
  * workspace) and the state scan; segments are sized to the workspace and the
  * state is carried between them.  Without one it runs the single fused kernel.
  */

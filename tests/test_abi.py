@@ -37,7 +37,7 @@ def test_library_exports_every_declared_symbol(lib):
 def test_abi_version_and_status_strings(lib):
     from gdn_b200 import _lib
     assert lib.gdn_abi_version() == _lib.ABI_VERSION
-    for code in range(0, 7):
+    for code in range(0, 8):
         assert len(lib.gdn_status_string(code)) > 0
     assert b"unknown" in lib.gdn_status_string(99)
 
@@ -74,6 +74,9 @@ def _args(**kw):
     ("chunk_size", 32, 2),
     ("block_v", 48, 2),
     ("q", 0x10008, 3),           # not 16-byte aligned
+    ("flags", 8, 1),             # unknown input-prep flag
+    ("scale", float("nan"), 1),
+    ("beta", None, 1),
 ])
 def test_validation_rejects_before_device_work(lib, field, value, expected):
     a = _args(**{field: value})
@@ -85,6 +88,17 @@ def test_null_input_pointer_rejected(lib):
     a = _args()
     a.v = None
     assert lib.gdn_fwd_sm100(ctypes.byref(a), None) == 1
+
+
+def test_null_gate_is_accepted(lib):
+    """g == NULL selects the DeltaNet recurrence (g == 0): validation passes and
+    the call gets as far as the device check."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present; covered by the GPU tests")
+    a = _args()
+    a.g = None
+    assert lib.gdn_fwd_sm100(ctypes.byref(a), None) == 6
 
 
 def test_misaligned_stride_rejected(lib):

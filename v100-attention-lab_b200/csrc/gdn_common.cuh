@@ -2,6 +2,7 @@
 // vector layout, operand writers and the fp32 unit-lower-triangular inverse.
 #pragma once
 #include "tc.cuh"
+#include "../../include/gdn_b200.h"
 
 namespace gdn {
 
@@ -25,6 +26,22 @@ constexpr int kTraceSlots = 24;
   do {                      \
   } while (0)
 #endif
+
+// beta and g of one step as the kernels use them: zero past T (the padding
+// rule of gdn_ref.py:102-114), g == 0 when no gate tensor is given (the
+// DeltaNet recurrence), and the activations of bench_gdn.py:33-40 applied here
+// when the inputs are logits (GDN_FLAG_BETA_SIGMOID, GDN_FLAG_G_LOGSIGMOID).
+__device__ __forceinline__ float load_beta(const float* bp, long long off, bool valid, int flags) {
+  if (!valid) return 0.f;
+  const float x = bp[off];
+  return (flags & GDN_FLAG_BETA_SIGMOID) ? 1.f / (1.f + expf(-x)) : x;
+}
+__device__ __forceinline__ float load_g(const float* gp, long long off, bool valid, int flags) {
+  if (!valid || gp == nullptr) return 0.f;
+  const float x = gp[off];
+  // logsigmoid(x) = min(x, 0) - log(1 + e^{-|x|})
+  return (flags & GDN_FLAG_G_LOGSIGMOID) ? fminf(x, 0.f) - log1pf(expf(-fabsf(x))) : x;
+}
 
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   uint32_t ok;

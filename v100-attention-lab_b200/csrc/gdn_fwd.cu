@@ -128,6 +128,8 @@ struct FwdParams {
   long long sg_b, sg_t, sg_h;
   long long so_b, so_t, so_h;
   int B, T, H, NT, nslice;
+  float scale;  // multiplies o (q scaled)
+  int flags;    // GDN_FLAG_BETA_SIGMOID / GDN_FLAG_G_LOGSIGMOID
 };
 
 // ------------------------------------------------------------------ kernel
@@ -183,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
   if (warp == 0) {
     // ================================================================ producer
     constexpr float kLog2e = 1.4426950408889634f;
-    const float* gp = P.g + bb * P.sg_b + hh * P.sg_h;
+    const float* gp = P.g == nullptr ? nullptr : P.g + bb * P.sg_b + hh * P.sg_h;
     const float* bp = P.beta + bb * P.sb_b + hh * P.sb_h;
     int issued = 0;
     for (int i = 0; i < NT; ++i) {
@@ -205,10 +207,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
       // beta and the in-chunk cumsum of g (log2 units); zero past T, which is
       // the padding rule of gdn_ref.py:102-114 (beta = g = 0).
       const int ta = t0 + lane, tb = t0 + lane + 32;
-      float xa = (ta < P.T) ? gp[(long long)ta * P.sg_t] * kLog2e : 0.f;
-      float xb = (tb < P.T) ? gp[(long long)tb * P.sg_t] * kLog2e : 0.f;
-      const float ba = (ta < P.T) ? bp[(long long)ta * P.sb_t] : 0.f;
-      const float bbv = (tb < P.T) ? bp[(long long)tb * P.sb_t] : 0.f;
+      float xa = load_g(gp, (long long)ta * P.sg_t, ta < P.T, P.flags) * kLog2e;
+      float xb = load_g(gp, (long long)tb * P.sg_t, tb < P.T, P.flags) * kLog2e;
+      const float ba = load_beta(bp, (long long)ta * P.sb_t, ta < P.T, P.flags);
+      const float bbv = load_beta(bp, (long long)tb * P.sb_t, tb < P.T, P.flags);
 #pragma unroll
       for (int d = 1; d < 32; d <<= 1) {
         const float ya = __shfl_up_sync(0xffffffffu, xa, d);
@@ -630,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_fwd_kernel(const __grid_const
           const int t = i * kC + r;
           if (r < 64 && t < P.T) {
 #pragma unroll
-            for (int j = 0; j < BV; ++j) z[j] += y[j];  // o = Qhat h^T + P u   (gdn_ref.py:89-90)
+            for (int j = 0; j < BV; ++j) z[j] = (z[j] + y[j]) * P.scale;  // o = Qhat h^T + P u   (gdn_ref.py:89-90)
             OutT* dst = reinterpret_cast<OutT*>(P.o) + bb * P.so_b + (long long)t * P.so_t + hh * P.so_h + v0;
             store_row<OutT>(dst, z, BV);
           }
@@ -688,7 +690,10 @@ int elem_size(int dt) { return dt == GDN_DTYPE_F32 ? 4 : 2; }
 int validate(const gdn_fwd_args* a, bool need_out) {
   if (a == nullptr || a->abi_version != GDN_B200_ABI_VERSION) return GDN_ERR_INVALID_ARGUMENT;
   if (a->B < 1 || a->T < 1 || a->H < 1 || a->K < 1 || a->V < 1) return GDN_ERR_INVALID_ARGUMENT;
-  if (!a->q || !a->k || !a->v || !a->beta || !a->g) return GDN_ERR_INVALID_ARGUMENT;
+  if (!a->q || !a->k || !a->v || !a->beta) return GDN_ERR_INVALID_ARGUMENT;  // g may be NULL (g == 0)
+  if (a->flags & ~(GDN_FLAG_QK_L2NORM | GDN_FLAG_BETA_SIGMOID | GDN_FLAG_G_LOGSIGMOID))
+    return GDN_ERR_INVALID_ARGUMENT;
+  if (!(a->scale == a->scale) || a->scale > 3.0e38f || a->scale < -3.0e38f) return GDN_ERR_INVALID_ARGUMENT;
   if (need_out && !a->o) return GDN_ERR_INVALID_ARGUMENT;
   if (a->in_dtype != GDN_DTYPE_F16 && a->in_dtype != GDN_DTYPE_BF16) {
     return (a->in_dtype == GDN_DTYPE_F32) ? GDN_ERR_UNSUPPORTED : GDN_ERR_INVALID_ARGUMENT;
@@ -790,6 +795,8 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
   wp.sg_b = a->g_stride[0];
   wp.sg_t = a->g_stride[1];
   wp.sg_h = a->g_stride[2];
+  wp.scale = a->scale == 0.f ? 1.f : a->scale;
+  wp.flags = a->flags;
   sp.so_b = a->o_stride[0];
   sp.so_t = a->o_stride[1];
   sp.so_h = a->o_stride[2];
@@ -837,6 +844,8 @@ int run(const gdn_fwd_args* a, float* w_out, float* u_out, void* stream, bool pr
     if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0 && a->workspace_bytes >= state_bytes + per_chunk)
       return run_two_kernel(a, stream, per_chunk, state_bytes);
   }
+  // the single fused kernel (and the WY/UT-only mode) reads q and k as given
+  if (a->flags & GDN_FLAG_QK_L2NORM) return GDN_ERR_UNSUPPORTED;
   FwdParams p;
   memset(&p, 0, sizeof(p));
   if (!make_input_map(&p.tm_q, a, a->q, a->q_stride, kK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -868,6 +877,8 @@ int run(const gdn_fwd_args* a, float* w_out, float* u_out, void* stream, bool pr
   p.H = a->H;
   p.NT = (a->T + kC - 1) / kC;
   p.nslice = kV / BV;
+  p.scale = a->scale == 0.f ? 1.f : a->scale;
+  p.flags = a->flags;
   const int grid = a->B * a->H * p.nslice;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a->in_dtype == GDN_DTYPE_BF16)

@@ -61,8 +61,8 @@ constexpr int kMmaWarp = 8;
 constexpr uint32_t k0 = 0, q0 = 8192, k1 = 16384, q1 = 24576;  // k later -> Kbar fp16 in place
 constexpr uint32_t v0 = 32768, v1 = 49152;                     // later U_lo fp16
 constexpr uint32_t p16 = 40960;    // P fp16, 64 x 128 B
-constexpr uint32_t tw = 57344;     // [Tw; Tb_hi] (input dtype): one M = 128 operand; later W fp16
-constexpr uint32_t zz = 73728;     // [0; Tb_lo]: one M = 128 operand; later U_hi fp16
+constexpr uint32_t tw = 57344;     // [Tw_hi; Tb_hi] (input dtype): one M = 128 operand; later W fp16
+constexpr uint32_t zz = 73728;     // [Tw_lo; Tb_lo]: one M = 128 operand; later U_hi fp16
 constexpr uint32_t amat = 90112;   // fp32 A / T (64 x kAStride); later o_intra staging
 constexpr uint32_t vec = amat + 17408;  // kVecN x 64 fp32
 constexpr uint32_t bars = vec + kVecN * kC * 4;
@@ -76,7 +76,7 @@ static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
 // Packet pieces are staged in shared memory that the finished MMAs no longer
 // read and leave in bulk copies: Q' in place over q, o_intra over A/T,
 // N over [W | U_hi], c over [Kbar | U_lo].
-enum { B_FULL = 0, B_SFULL, B_TREADY, B_WUFULL, B_EPA, B_PFULL, B_EPC, B_NCFULL, B_DONE, B_COUNT };
+enum { B_FULL = 0, B_SFULL, B_TREADY, B_WUFULL, B_EPA, B_PFULL, B_EPC, B_NCFULL, B_DONE, B_NORM, B_COUNT };
 }  // namespace wy
 
 __device__ __forceinline__ uint4 pack8_f16(const float* x) {
@@ -120,7 +120,9 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
 
   if (tid == 0) {
     for (int i = 0; i < wy::B_COUNT; ++i)
-      mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC) ? wy::kPrep / 32 : 1);
+      mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC || i == wy::B_NORM)
+                              ? wy::kPrep / 32
+                              : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -168,11 +170,11 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     }
     // in-chunk cumsum of g (log2 units) and beta; zero past T (gdn_ref.py:102-114)
     constexpr float kLog2e = 1.4426950408889634f;
-    const float* gp = P.g + bb * P.sg_b + hh * P.sg_h;
+    const float* gp = P.g == nullptr ? nullptr : P.g + bb * P.sg_b + hh * P.sg_h;
     const float* bp = P.beta + bb * P.sb_b + hh * P.sb_h;
     const int ta = t0 + lane, tb = t0 + lane + 32;
-    float xa = (ta < P.T) ? gp[(long long)ta * P.sg_t] * kLog2e : 0.f;
-    float xb = (tb < P.T) ? gp[(long long)tb * P.sg_t] * kLog2e : 0.f;
+    float xa = load_g(gp, (long long)ta * P.sg_t, ta < P.T, P.flags) * kLog2e;
+    float xb = load_g(gp, (long long)tb * P.sg_t, tb < P.T, P.flags) * kLog2e;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const float ya = __shfl_up_sync(0xffffffffu, xa, d);
@@ -186,8 +188,8 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     const float bC = __shfl_sync(0xffffffffu, xb, 31);
     vec[V_B2 * kC + lane] = xa;
     vec[V_B2 * kC + lane + 32] = xb;
-    vec[V_BETA * kC + lane] = (ta < P.T) ? bp[(long long)ta * P.sb_t] : 0.f;
-    vec[V_BETA * kC + lane + 32] = (tb < P.T) ? bp[(long long)tb * P.sb_t] : 0.f;
+    vec[V_BETA * kC + lane] = load_beta(bp, (long long)ta * P.sb_t, ta < P.T, P.flags);
+    vec[V_BETA * kC + lane + 32] = load_beta(bp, (long long)tb * P.sb_t, tb < P.T, P.flags);
     vec[V_EB * kC + lane] = fast_exp2(xa);
     vec[V_EB * kC + lane + 32] = fast_exp2(xb);
     vec[V_DD * kC + lane] = fast_exp2(bC - xa);
@@ -200,6 +202,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
   if (warp == wy::kMmaWarp) {
     // ------------------------------------------------ MMA issue (the whole warp; elect.sync inside)
     ok = mbar_wait_warp(&bars[wy::B_FULL], 0, abort_flag);
+    if (P.flags & GDN_FLAG_QK_L2NORM) ok = ok && mbar_wait_warp(&bars[wy::B_NORM], 0, abort_flag);
     if (lane == 0) WY_TR(1);
     if (ok) {
       // S = [K;Q] K^T: M=128 (k rows then q rows), N=64, K=128
@@ -214,19 +217,17 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       ok = mbar_wait_warp(&bars[wy::B_TREADY], 0, abort_flag);
     }
     if (ok) {
-      // [Tw; Tb_hi] [K | V] (M=128, N=256, K=64), then [0; Tb_lo] V into cols 128-255:
-      // W = lanes 0-63 x cols 0-127, U = Tb_hi V + Tb_lo V = lanes 64-127 x cols 128-255
+      // ([Tw_hi; Tb_hi] + [Tw_lo; Tb_lo]) [K | V] (M=128, N=256, K=64 twice):
+      // W = lanes 0-63 x cols 0-127, U = lanes 64-127 x cols 128-255.  Both T
+      // operands are split hi + lo in the input dtype: with bf16 inputs one
+      // 8-bit-mantissa copy of T alone costs ~1e-3 on the final state when g is
+      // small (slow decay keeps every chunk's error).
       tc_fence_after();
       const uint32_t id_wu = idesc_f16(128, 256, kInBf16, 0, 1);
-      const uint32_t id_lo = idesc_f16(128, 128, kInBf16, 0, 1);
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss_warp(tmem, sdesc(sb + wy::tw + kk * 32, 16, 1024, kSw128),
-                        sdesc(sb + wy::k0 + kk * 2048, 16384, 1024, kSw128), id_wu, kk > 0);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::zz + kk * 32, 16, 1024, kSw128),
-                        sdesc(sb + wy::v0 + kk * 2048, 16384, 1024, kSw128), id_lo, 1);
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_ss_warp(tmem, sdesc(sb + (kk < 4 ? wy::tw : wy::zz) + (kk & 3) * 32, 16, 1024, kSw128),
+                        sdesc(sb + wy::k0 + (kk & 3) * 2048, 16384, 1024, kSw128), id_wu, kk > 0);
       mma_commit_warp(&bars[wy::B_WUFULL]);
       ok = mbar_wait_warp(&bars[wy::B_EPA], 0, abort_flag);
     }
@@ -276,6 +277,43 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     const bool prod_form = (b2first - b2last) < 200.f;
     if (ptid < 64) amat[ptid * kAStride + 64] = fast_exp2(ref - vec[V_B2 * kC + ptid]);
     named_bar(2, NP);
+    if (P.flags & GDN_FLAG_QK_L2NORM) {
+      // raw q and k: every row divided by sqrt(sum of squares + 1e-6) in fp32, in
+      // place, before any product reads them (gdn_ref.py:24-25).  Thread pair
+      // (2i, 2i+1) takes the two 64-column blocks of row i (k rows, then q rows).
+      if (mbar_wait_warp(&bars[wy::B_FULL], 0, abort_flag)) {
+        const int rr = ptid >> 1, half = ptid & 1, t = rr & 63;
+        uint8_t* blk = sm + (rr < 64 ? wy::k0 : wy::q0) + half * 16384;
+        uint4 xv[8];
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          xv[c] = *reinterpret_cast<const uint4*>(blk + sw128_off(t, c));
+          const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = Cvt<InT>::unpack(w4[e]);
+            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+          }
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        const float inv = 1.f / sqrtf(ss + 1e-6f);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+          uint32_t y4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = Cvt<InT>::unpack(w4[e]);
+            y4[e] = Cvt<InT>::pack(f.x * inv, f.y * inv);
+          }
+          *reinterpret_cast<uint4*>(blk + sw128_off(t, c)) = make_uint4(y4[0], y4[1], y4[2], y4[3]);
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[wy::B_NORM]);
+    }
     ok = mbar_wait_warp(&bars[wy::B_SFULL], 0, abort_flag);
     if (ptid == 0) WY_TR(2);
     if (bar_any(1, NP, !ok || *abort_flag)) ok = false;
@@ -315,32 +353,36 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       if (ptid == 0) WY_TR(3);
       invert_unit_lower64<NP>(amat, ptid);  // T = (I + A)^-1 in place
       if (ptid == 0) WY_TR(4);
-      // Tw = T diag(beta e^b) -> [Tw; .]; Tb = T diag(beta) -> hi [.; Tb_hi] + lo [0; Tb_lo]
+      // Tw = T diag(beta e^b), Tb = T diag(beta), each split hi + lo in the input dtype:
+      // [Tw_hi; Tb_hi] and [Tw_lo; Tb_lo]
       {
         const int rr = ptid >> 2, cq = ptid & 3;
         const float* trow = amat + rr * kAStride;
-        uint8_t* twp = sm + wy::tw;
-        uint8_t* hip = sm + wy::tw + 8192;
-        uint8_t* lop = sm + wy::zz + 8192;
+        uint8_t* twh = sm + wy::tw;
+        uint8_t* tbh = sm + wy::tw + 8192;
+        uint8_t* twl = sm + wy::zz;
+        uint8_t* tbl = sm + wy::zz + 8192;
 #pragma unroll
         for (int c = 2 * cq; c < 2 * cq + 2; ++c) {
-          uint32_t ww[4], hi[4], lo[4];
+          uint32_t wh[4], wl[4], hi[4], lo[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int m = 8 * c + 2 * e;
             const float tb0 = trow[m] * vec[V_BETA * kC + m], tb1 = trow[m + 1] * vec[V_BETA * kC + m + 1];
-            ww[e] = Cvt<InT>::pack(tb0 * vec[V_EB * kC + m], tb1 * vec[V_EB * kC + m + 1]);
+            const float tw0 = tb0 * vec[V_EB * kC + m], tw1 = tb1 * vec[V_EB * kC + m + 1];
+            wh[e] = Cvt<InT>::pack(tw0, tw1);
+            const float2 wf = Cvt<InT>::unpack(wh[e]);
+            wl[e] = Cvt<InT>::pack(tw0 - wf.x, tw1 - wf.y);
             hi[e] = Cvt<InT>::pack(tb0, tb1);
             const float2 hf = Cvt<InT>::unpack(hi[e]);
             lo[e] = Cvt<InT>::pack(tb0 - hf.x, tb1 - hf.y);
           }
-          *reinterpret_cast<uint4*>(twp + sw128_off(rr, c)) = make_uint4(ww[0], ww[1], ww[2], ww[3]);
-          *reinterpret_cast<uint4*>(hip + sw128_off(rr, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-          *reinterpret_cast<uint4*>(lop + sw128_off(rr, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          const uint32_t off = sw128_off(rr, c);
+          *reinterpret_cast<uint4*>(twh + off) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+          *reinterpret_cast<uint4*>(twl + off) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+          *reinterpret_cast<uint4*>(tbh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(tbl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
-        // the zero upper half of [0; Tb_lo]
-        *reinterpret_cast<uint4*>(sm + wy::zz + ptid * 32) = make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(sm + wy::zz + ptid * 32 + 16) = make_uint4(0u, 0u, 0u, 0u);
       }
       fence_async_smem();
       __syncwarp();
@@ -348,7 +390,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       if (ptid == 0) WY_TR(5);
     }
     // ---- epilogue A: rows 0-63 W -> fp16 [t][k] (over [Tw; Tb_hi]); rows 64-127 U -> fp16
-    //      hi (over [0; Tb_lo]) and lo (over v); and k -> Kbar = e^{b_C - b_t} k fp16 in place
+    //      hi (over [Tw_lo; Tb_lo]) and lo (over v); and k -> Kbar = e^{b_C - b_t} k fp16 in place
     ok = ok && mbar_wait_warp(&bars[wy::B_WUFULL], 0, abort_flag);
     if (ptid == 0) WY_TR(6);
     if (ok) {
@@ -429,8 +471,8 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 f = Cvt<InT>::unpack(xs[e]);
-              y[2 * e] = fmaf(eb, f.x, -pw[8 * c + 2 * e]);
-              y[2 * e + 1] = fmaf(eb, f.y, -pw[8 * c + 2 * e + 1]);
+              y[2 * e] = fmaf(eb, f.x, -pw[8 * c + 2 * e]) * P.scale;
+              y[2 * e + 1] = fmaf(eb, f.y, -pw[8 * c + 2 * e + 1]) * P.scale;
             }
             *pp = pack8_f16(y);
           }
@@ -443,7 +485,12 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         if (lane < 16) {
           uint8_t* dst = sm + wy::amat + (c0 >> 5) * 4096;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + sw64_off(t, c)) = pack8_f16(ou + 8 * c);
+          for (int c = 0; c < 4; ++c) {
+            float sc8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sc8[e] = ou[8 * c + e] * P.scale;
+            *reinterpret_cast<uint4*>(dst + sw64_off(t, c)) = pack8_f16(sc8);
+          }
         }
       }
       tc_fence_before();

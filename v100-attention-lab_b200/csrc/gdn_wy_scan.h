@@ -18,6 +18,8 @@ struct WyParams {
   long long sb_b, sb_t, sb_h;
   long long sg_b, sg_t, sg_h;
   int B, T, H, c0, NS;  // segment = chunks [c0, c0 + NS)
+  float scale;          // multiplies Q' and o_intra (q scaled)
+  int flags;            // GDN_FLAG_*
   int pf_stride;        // CTAs resident at once (2 per SM): blockIdx + pf_stride is prefetched to L2
 };
 

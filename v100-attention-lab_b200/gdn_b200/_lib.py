@@ -12,7 +12,7 @@ import threading
 
 from . import _build
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 DTYPE_F32 = 0
 DTYPE_F16 = 1
@@ -26,6 +26,11 @@ ERR_CUDA = 4
 ERR_TIMEOUT = 5
 ERR_NO_DEVICE = 6
 ERR_SCRATCH_LIMIT = 7
+
+# gdn_fwd_args.flags: input preparation inside the kernel
+FLAG_QK_L2NORM = 1
+FLAG_BETA_SIGMOID = 2
+FLAG_G_LOGSIGMOID = 4
 
 # Scratch bytes of the two-kernel path per (batch, head, chunk of 64 steps);
 # gdn_fwd_workspace_bytes() is the authority, this mirrors it for sizing.
@@ -69,6 +74,8 @@ class GdnFwdArgs(ctypes.Structure):
         ("status", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_uint64),
+        ("scale", ctypes.c_float),
+        ("flags", ctypes.c_int32),
     ]
 
 

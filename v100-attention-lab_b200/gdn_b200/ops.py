@@ -75,7 +75,9 @@ def check_status(device=None) -> None:
 
 
 def _check_inputs(q, k, v, beta, g):
-    tensors = {"q": q, "k": k, "v": v, "beta": beta, "g": g}
+    tensors = {"q": q, "k": k, "v": v, "beta": beta}
+    if g is not None:
+        tensors["g"] = g
     for name, t in tensors.items():
         if not isinstance(t, torch.Tensor):
             raise TypeError(f"{name} must be a torch.Tensor")
@@ -86,7 +88,7 @@ def _check_inputs(q, k, v, beta, g):
         raise ValueError(f"k shape {tuple(k.shape)} != q shape {tuple(q.shape)}")
     if tuple(v.shape[:3]) != (B, T, H):
         raise ValueError(f"v shape {tuple(v.shape)} does not match q's [B, T, H]")
-    if tuple(beta.shape) != (B, T, H) or tuple(g.shape) != (B, T, H):
+    if tuple(beta.shape) != (B, T, H) or (g is not None and tuple(g.shape) != (B, T, H)):
         raise ValueError(f"beta and g must be [B, T, H] = {(B, T, H)}")
     if q.dtype != k.dtype or q.dtype != v.dtype:
         raise ValueError(f"q, k, v must share a dtype (got {q.dtype}, {k.dtype}, {v.dtype})")
@@ -104,7 +106,7 @@ def _check_inputs(q, k, v, beta, g):
     return B, T, H, K, v.shape[-1]
 
 
-def _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status) -> _lib.GdnFwdArgs:
+def _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status, scale=1.0, flags=0) -> _lib.GdnFwdArgs:
     B, T, H, K = q.shape
     a = _lib.GdnFwdArgs()
     a.abi_version = _lib.ABI_VERSION
@@ -114,6 +116,8 @@ def _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status) -> _lib
     a.out_dtype = _DTYPES[o.dtype] if o is not None else _lib.DTYPE_F32
     a.block_v = int(block_v)
     for name, t in (("q", q), ("k", k), ("v", v), ("beta", beta), ("g", g)):
+        if t is None:  # g: no gate (g == 0)
+            continue
         setattr(a, name, t.data_ptr())
         st = getattr(a, name + "_stride")
         st[0], st[1], st[2] = t.stride(0), t.stride(1), t.stride(2)
@@ -123,18 +127,37 @@ def _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status) -> _lib
         a.o_stride[0], a.o_stride[1], a.o_stride[2] = o.stride(0), o.stride(1), o.stride(2)
     a.ht = ht.data_ptr() if ht is not None else None
     a.status = status.data_ptr() if status is not None else None
+    a.scale = float(scale)
+    a.flags = int(flags)
     return a
 
 
+def _prep_flags(use_qk_l2norm_in_kernel, beta_activation, g_activation):
+    flags = 0
+    if use_qk_l2norm_in_kernel:
+        flags |= _lib.FLAG_QK_L2NORM
+    if beta_activation is not None:
+        if beta_activation != "sigmoid":
+            raise ValueError(f"beta_activation must be None or 'sigmoid' (got {beta_activation!r})")
+        flags |= _lib.FLAG_BETA_SIGMOID
+    if g_activation is not None:
+        if g_activation != "logsigmoid":
+            raise ValueError(f"g_activation must be None or 'logsigmoid' (got {g_activation!r})")
+        flags |= _lib.FLAG_G_LOGSIGMOID
+    return flags
+
+
 def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output_dtype=None,
-                  output_final_state=True, block_v=0, check=False, fused=False):
+                  output_final_state=True, block_v=0, check=False, fused=False, scale=None,
+                  use_qk_l2norm_in_kernel=False, beta_activation=None, g_activation=None):
     """Chunked Gated DeltaNet forward on a B200.
 
     Args:
         q, k: [B, T, H, K] fp16/bf16 (last dim contiguous)
         v:    [B, T, H, V] same dtype
         beta: [B, T, H] (cast to fp32 if needed)
-        g:    [B, T, H] log decay (<= 0), cast to fp32 if needed
+        g:    [B, T, H] log decay (<= 0), cast to fp32 if needed; None means
+              g == 0 (no decay: the DeltaNet recurrence)
         initial_state: optional [B, H, V, K] state h0 (fp32 is used)
         chunk_size: C (this build: 64)
         output_dtype: dtype of o (default q.dtype, as gdn_triton.py:126)
@@ -142,8 +165,14 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
         block_v: V columns per CTA (0 = choose)
         check: synchronise and raise if the kernel reported an error
         fused: run the single fused kernel instead of the two-kernel path
-            (chunk-parallel WY/UT preparation + state scan); both give the
-            same results, the fused one needs no scratch memory
+            (chunk-parallel WY/UT preparation + state scan); both meet the
+            same tolerance, the fused one needs no scratch memory
+        scale: q is scaled by this factor (the FLA convention); None = 1,
+            the reference's behaviour
+        use_qk_l2norm_in_kernel: q and k are raw; their rows are
+            L2-normalised inside the kernel (gdn_ref.py:24-25), fp32 math
+        beta_activation: 'sigmoid' if beta holds logits
+        g_activation: 'logsigmoid' if g holds logits
     Returns:
         (o [B, T, H, V], h_final [B, H, V, K] fp32 or None)
 
@@ -152,10 +181,14 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
     gdn_triton.py:122-125.
     """
     B, T, H, K, V = _check_inputs(q, k, v, beta, g)
+    flags = _prep_flags(use_qk_l2norm_in_kernel, beta_activation, g_activation)
+    if g is None and g_activation is not None:
+        raise ValueError("g_activation needs a g tensor")
+    scale = 1.0 if scale is None else float(scale)
     lib = _lib.load()
     dev = q.device
     beta = beta if beta.dtype == torch.float32 else beta.float()
-    g = g if g.dtype == torch.float32 else g.float()
+    g = g if (g is None or g.dtype == torch.float32) else g.float()
     h0 = None
     if initial_state is not None:
         if tuple(initial_state.shape) != (B, H, V, K):
@@ -169,7 +202,7 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
     o = torch.empty(B, T, H, V, dtype=out_dtype, device=dev)
     ht = torch.empty(B, H, V, K, dtype=torch.float32, device=dev) if output_final_state else None
     status = _status_word(dev)
-    args = _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status)
+    args = _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status, scale, flags)
     if not fused:
         need = int(lib.gdn_fwd_workspace_bytes(ctypes.byref(args)))
         per_head = B * H * (_lib.PACKET_BYTES_PER_CHUNK + V * K * 4)
