@@ -58,6 +58,16 @@ enum gdn_status {
 #define GDN_FLAG_QK_L2NORM 1
 #define GDN_FLAG_BETA_SIGMOID 2
 #define GDN_FLAG_G_LOGSIGMOID 4
+/*
+ * Solver of (I + A)^-1 per chunk.  Default: exact, fp32 (blocked forward
+ * substitution, the role of gdn_triton.py:75-84).  GDN_FLAG_SOLVER_NS selects
+ * the Newton-Schulz iteration of gdn_triton_v2.py:58-68 (fp16 tensor-core
+ * products, approximate) with GDN_FLAG_NS_ITERS(n) iterations, 1 <= n <= 15;
+ * two-kernel path only.
+ */
+#define GDN_FLAG_SOLVER_NS 8
+#define GDN_FLAG_NS_ITERS_SHIFT 8
+#define GDN_FLAG_NS_ITERS(n) ((int32_t)(n) << GDN_FLAG_NS_ITERS_SHIFT)
 
 /*
  * Arguments of one forward call.  Shapes follow the reference

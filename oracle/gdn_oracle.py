@@ -44,7 +44,7 @@ from __future__ import annotations
 
 import numpy as np
 
-__all__ = ["l2norm", "recurrent", "chunked", "pad_to_multiple", "chunk_stages",
+__all__ = ["l2norm", "recurrent", "chunked", "pad_to_multiple", "chunk_stages", "ns_inverse",
            "make_inputs", "max_rel"]
 
 
@@ -94,11 +94,40 @@ def _unit_lower_solve(M, R):
     return X
 
 
-def chunk_stages(kc, vc, bc, gc, dtype=np.float64):
+def _f16(x):
+    return np.asarray(x).astype(np.float16).astype(np.float64)
+
+
+def ns_inverse(A, iters, final_fp32=True):
+    """(I + A)^-1 by the Newton-Schulz iteration of ``gdn_triton_v2.py:58-63``.
+
+    M = I + A and X = I - A are rounded to fp16; each of ``iters`` steps forms
+    M X with fp32 accumulation, rounds 2I - M X to fp16 and sets X to
+    X (2I - M X), again accumulated in fp32 and rounded to fp16.  The
+    reference keeps the last X in fp16 as well; ``final_fp32=True`` keeps the
+    last product in fp32, as the B200 kernel does before it splits T into a
+    hi + lo pair.  The error falls as A^(2^(iters+1)) (zero once
+    2^(iters+1) >= C) until the fp16 roundings bound it.
+    """
+    A = np.asarray(A, dtype=np.float64)
+    eye = np.broadcast_to(np.eye(A.shape[-1]), A.shape)
+    m16 = _f16(eye + A)
+    x = _f16(eye - A)
+    for i in range(iters):
+        y = _f16(2.0 * eye - (m16 @ x).astype(np.float32))
+        x = (x @ y).astype(np.float32).astype(np.float64)
+        if i + 1 < iters or not final_fp32:
+            x = _f16(x)
+    return x
+
+
+def chunk_stages(kc, vc, bc, gc, dtype=np.float64, ns_iters=None):
     """Per-chunk, state-independent quantities of ``gdn_ref.py:76-85``.
 
     kc [..., C, K], vc [..., C, V], bc/gc [..., C].  Returns a dict with
-    b (cumsum of g), A (strictly lower), Tinv = (I+A)^-1, U and W.
+    b (cumsum of g), A (strictly lower), Tinv = (I+A)^-1, U and W.  With
+    ``ns_iters`` set, Tinv comes from ``ns_inverse`` (the v2 solver) instead
+    of exact forward substitution.
     """
     kc = kc.astype(dtype); vc = vc.astype(dtype)
     bc = bc.astype(dtype); gc = gc.astype(dtype)
@@ -108,17 +137,18 @@ def chunk_stages(kc, vc, bc, gc, dtype=np.float64):
     dec = np.exp(b[..., :, None] - b[..., None, :])
     A = np.tril(kk * dec * bc[..., :, None], -1)
     eye = np.broadcast_to(np.eye(C, dtype=dtype), A.shape)
-    Tinv = _unit_lower_solve(eye + A, eye)
+    Tinv = _unit_lower_solve(eye + A, eye) if ns_iters is None else ns_inverse(A, ns_iters).astype(dtype)
     U = Tinv @ (vc * bc[..., None])
     W = Tinv @ (kc * (bc * np.exp(b))[..., None])
     return {"b": b, "A": A, "Tinv": Tinv, "U": U, "W": W, "dec": dec}
 
 
 def chunked(q, k, v, beta, g, C=64, initial_state=None, dtype=np.float64,
-            fold_state=True):
+            fold_state=True, ns_iters=None):
     """Chunked UT-transform forward (``gdn_ref.py:48-99``).
 
     T must be a multiple of C (``gdn_ref.py:62``); use ``pad_to_multiple``.
+    ``ns_iters`` selects the Newton-Schulz solve (``ns_inverse``).
     Returns (o [B,T,H,V], h_final [B,H,V,K]) in ``dtype``.
     """
     q = _as(q, dtype); k = _as(k, dtype); v = _as(v, dtype)
@@ -137,7 +167,7 @@ def chunked(q, k, v, beta, g, C=64, initial_state=None, dtype=np.float64,
         vc = v[:, c0:c0 + C].transpose(0, 2, 1, 3)
         bc = beta[:, c0:c0 + C].transpose(0, 2, 1)
         gc = g[:, c0:c0 + C].transpose(0, 2, 1)
-        st = chunk_stages(kc, vc, bc, gc, dtype)
+        st = chunk_stages(kc, vc, bc, gc, dtype, ns_iters)
         b, U, W, dec = st["b"], st["U"], st["W"], st["dec"]
         u = U - np.einsum("bhck,bhvk->bhcv", W, h)
         P = np.tril((qc @ np.swapaxes(kc, -1, -2)) * dec)
@@ -173,15 +203,19 @@ def pad_to_multiple(q, k, v, beta, g, C):
     return padt(q), padt(k), padt(v), padt(beta), padt(g)
 
 
-def make_inputs(B, T, H, K, V, seed=0, gate_mean=0.0, h0_std=None):
+def make_inputs(B, T, H, K, V, seed=0, gate_mean=0.0, h0_std=None, key_corr=0.0):
     """Seeded synthetic float32 inputs with the BASELINE distributions.
 
     q, k = l2norm(N(0,1)) along K; v = N(0,1); beta = sigmoid(N(0,1));
     g = logsigmoid(N(gate_mean, 1)); h0 = N(0, h0_std) or None.
+    ``key_corr`` > 0 adds key_corr times a per-head direction c ~ N(0,1)^K to
+    every key before its normalisation, so that keys correlate as in trained
+    models and the entries of A grow (0.56 at most for key_corr = 2 instead
+    of 0.12); the other inputs keep the same draws.
     """
     rng = np.random.default_rng(seed)
     q = l2norm(rng.standard_normal((B, T, H, K), dtype=np.float32))
-    k = l2norm(rng.standard_normal((B, T, H, K), dtype=np.float32))
+    k_raw = rng.standard_normal((B, T, H, K), dtype=np.float32)
     v = rng.standard_normal((B, T, H, V), dtype=np.float32)
     z = rng.standard_normal((B, T, H), dtype=np.float32)
     beta = (1.0 / (1.0 + np.exp(-z))).astype(np.float32)
@@ -190,7 +224,9 @@ def make_inputs(B, T, H, K, V, seed=0, gate_mean=0.0, h0_std=None):
     h0 = None
     if h0_std is not None:
         h0 = (rng.standard_normal((B, H, V, K), dtype=np.float32) * np.float32(h0_std))
-    return q, k, v, beta, g, h0
+    if key_corr:
+        k_raw = k_raw + np.float32(key_corr) * rng.standard_normal((1, 1, H, K), dtype=np.float32)
+    return q, l2norm(k_raw), v, beta, g, h0
 
 
 def max_rel(x, ref):

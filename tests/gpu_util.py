@@ -15,20 +15,22 @@ TOL = 1e-3
 STORE_ROUNDING = {torch.float32: 0.0, torch.float16: 2.0 ** -11, torch.bfloat16: 2.0 ** -8}
 
 
-def make(B, T, H, K=128, V=128, seed=0, dtype=torch.bfloat16, h0_std=None, gate_mean=0.0, dev="cuda"):
-    q, k, v, beta, g, h0 = ora.make_inputs(B, T, H, K, V, seed=seed, gate_mean=gate_mean, h0_std=h0_std)
+def make(B, T, H, K=128, V=128, seed=0, dtype=torch.bfloat16, h0_std=None, gate_mean=0.0, dev="cuda", key_corr=0.0):
+    q, k, v, beta, g, h0 = ora.make_inputs(B, T, H, K, V, seed=seed, gate_mean=gate_mean, h0_std=h0_std,
+                                           key_corr=key_corr)
     t = lambda x, dt=torch.float32: torch.from_numpy(np.ascontiguousarray(x)).to(dev).to(dt)
     qd, kd, vd = t(q, dtype), t(k, dtype), t(v, dtype)
     h0d = t(h0) if h0 is not None else None
     return qd, kd, vd, t(beta), t(g), h0d
 
 
-def oracle(qd, kd, vd, bd, gd, h0d, chunked=False, C=64):
-    """fp64 oracle on exactly the (16-bit-rounded) device inputs."""
+def oracle(qd, kd, vd, bd, gd, h0d, chunked=False, C=64, ns_iters=None):
+    """fp64 oracle on exactly the (16-bit-rounded) device inputs (chunked with
+    the Newton-Schulz solve when ns_iters is given)."""
     f = lambda x: None if x is None else x.float().cpu().numpy()
-    if chunked:
+    if chunked or ns_iters is not None:
         q, k, v, b, g = ora.pad_to_multiple(f(qd), f(kd), f(vd), f(bd), f(gd), C)
-        o, h = ora.chunked(q, k, v, b, g, C=C, initial_state=f(h0d))
+        o, h = ora.chunked(q, k, v, b, g, C=C, initial_state=f(h0d), ns_iters=ns_iters)
         return o[:, : qd.shape[1]], h
     return ora.recurrent(f(qd), f(kd), f(vd), f(bd), f(gd), initial_state=f(h0d))
 

@@ -74,7 +74,9 @@ def _args(**kw):
     ("chunk_size", 32, 2),
     ("block_v", 48, 2),
     ("q", 0x10008, 3),           # not 16-byte aligned
-    ("flags", 8, 1),             # unknown input-prep flag
+    ("flags", 16, 1),            # unknown flag
+    ("flags", 8, 1),             # Newton-Schulz without an iteration count
+    ("flags", 3 << 8, 1),        # an iteration count without Newton-Schulz
     ("scale", float("nan"), 1),
     ("beta", None, 1),
 ])

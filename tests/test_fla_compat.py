@@ -21,6 +21,11 @@ def test_prep_flags():
         ops._prep_flags(False, "relu", None)
     with pytest.raises(ValueError):
         ops._prep_flags(False, None, "softplus")
+    assert ops._prep_flags(False, None, None, "newton_schulz", 3) == _lib.FLAG_SOLVER_NS | (3 << _lib.NS_ITERS_SHIFT)
+    with pytest.raises(ValueError):
+        ops._prep_flags(False, None, None, "newton_schulz", 0)
+    with pytest.raises(ValueError):
+        ops._prep_flags(False, None, None, "cholesky")
 
 
 def test_grouped_value_heads_not_supported():

@@ -110,3 +110,26 @@ def test_planted_mistake_is_caught():
     g_shift = np.roll(g, 1, axis=1)
     o_bad, _ = ora.recurrent(q, k, v, b, g_shift)
     assert ora.max_rel(o_bad, o_r) > 1e-3
+
+
+def test_newton_schulz_restatement():
+    """ns_inverse follows gdn_triton_v2.py:58-63: X0 = I - A and
+    X <- X (2I - (I + A) X), so after one step I - (I + A) X = A^4 and after n
+    steps A^(2^(n+1)), up to the fp16 roundings; the error vs the exact
+    inverse falls until those roundings bound it."""
+    q, k, v, b, g, _ = ora.make_inputs(1, 128, 2, 128, 16, seed=5, key_corr=2.0)
+    st = ora.chunk_stages(k[:, :64].transpose(0, 2, 1, 3), v[:, :64].transpose(0, 2, 1, 3),
+                          b[:, :64].transpose(0, 2, 1), g[:, :64].transpose(0, 2, 1))
+    A, Tinv = st["A"], st["Tinv"]
+    eye = np.eye(64)
+    assert np.abs(A).max() > 0.3            # large enough for the iterations to matter
+    x1 = ora.ns_inverse(A, 1)
+    a4 = np.linalg.matrix_power(A[0, 0], 4)
+    assert np.abs((eye - (eye + A[0, 0]) @ x1[0, 0]) - a4).max() < 4e-3 * np.abs(a4).max() + 2e-3
+    errs = [ora.max_rel(ora.ns_inverse(A, n), Tinv) for n in range(1, 7)]
+    assert errs[0] > 10 * errs[1] > 10 * errs[2]
+    assert max(errs[2:]) < 1e-3              # fp16 floor from the third step on (A^16 is below it)
+    # exact solver path of the chunked oracle unchanged; NS path converges to it
+    o_ex, _ = ora.chunked(q, k, v, b, g)
+    o_ns, _ = ora.chunked(q, k, v, b, g, ns_iters=5)
+    assert 0 < ora.max_rel(o_ns, o_ex) < 1e-3

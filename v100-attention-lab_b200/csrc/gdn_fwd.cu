@@ -691,8 +691,13 @@ int validate(const gdn_fwd_args* a, bool need_out) {
   if (a == nullptr || a->abi_version != GDN_B200_ABI_VERSION) return GDN_ERR_INVALID_ARGUMENT;
   if (a->B < 1 || a->T < 1 || a->H < 1 || a->K < 1 || a->V < 1) return GDN_ERR_INVALID_ARGUMENT;
   if (!a->q || !a->k || !a->v || !a->beta) return GDN_ERR_INVALID_ARGUMENT;  // g may be NULL (g == 0)
-  if (a->flags & ~(GDN_FLAG_QK_L2NORM | GDN_FLAG_BETA_SIGMOID | GDN_FLAG_G_LOGSIGMOID))
-    return GDN_ERR_INVALID_ARGUMENT;
+  {
+    const int known = GDN_FLAG_QK_L2NORM | GDN_FLAG_BETA_SIGMOID | GDN_FLAG_G_LOGSIGMOID | GDN_FLAG_SOLVER_NS |
+                      GDN_FLAG_NS_ITERS(15);
+    if (a->flags & ~known) return GDN_ERR_INVALID_ARGUMENT;
+    const int iters = (a->flags >> GDN_FLAG_NS_ITERS_SHIFT) & 15;
+    if ((a->flags & GDN_FLAG_SOLVER_NS) ? iters == 0 : iters != 0) return GDN_ERR_INVALID_ARGUMENT;
+  }
   if (!(a->scale == a->scale) || a->scale > 3.0e38f || a->scale < -3.0e38f) return GDN_ERR_INVALID_ARGUMENT;
   if (need_out && !a->o) return GDN_ERR_INVALID_ARGUMENT;
   if (a->in_dtype != GDN_DTYPE_F16 && a->in_dtype != GDN_DTYPE_BF16) {
@@ -844,8 +849,9 @@ int run(const gdn_fwd_args* a, float* w_out, float* u_out, void* stream, bool pr
     if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0 && a->workspace_bytes >= state_bytes + per_chunk)
       return run_two_kernel(a, stream, per_chunk, state_bytes);
   }
-  // the single fused kernel (and the WY/UT-only mode) reads q and k as given
-  if (a->flags & GDN_FLAG_QK_L2NORM) return GDN_ERR_UNSUPPORTED;
+  // the single fused kernel (and the WY/UT-only mode) reads q and k as given and
+  // solves with the exact blocked inverse
+  if (a->flags & (GDN_FLAG_QK_L2NORM | GDN_FLAG_SOLVER_NS)) return GDN_ERR_UNSUPPORTED;
   FwdParams p;
   memset(&p, 0, sizeof(p));
   if (!make_input_map(&p.tm_q, a, a->q, a->q_stride, kK, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||

@@ -76,7 +76,8 @@ static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
 // Packet pieces are staged in shared memory that the finished MMAs no longer
 // read and leave in bulk copies: Q' in place over q, o_intra over A/T,
 // N over [W | U_hi], c over [Kbar | U_lo].
-enum { B_FULL = 0, B_SFULL, B_TREADY, B_WUFULL, B_EPA, B_PFULL, B_EPC, B_NCFULL, B_DONE, B_NORM, B_COUNT };
+enum { B_FULL = 0, B_SFULL, B_TREADY, B_WUFULL, B_EPA, B_PFULL, B_EPC, B_NCFULL, B_DONE, B_NORM, B_NSR, B_NSD,
+       B_COUNT };
 }  // namespace wy
 
 __device__ __forceinline__ uint4 pack8_f16(const float* x) {
@@ -86,6 +87,80 @@ __device__ __forceinline__ uint4 pack8_f16(const float* x) {
   w.z = Cvt<__half>::pack(x[4], x[5]);
   w.w = Cvt<__half>::pack(x[6], x[7]);
   return w;
+}
+
+// Newton-Schulz alternative to invert_unit_lower64, after gdn_triton_v2.py:58-68:
+// M = I + A and X = I - A as fp16 operands, then `iters` times
+//     Y = 2I - M X,   X = X Y
+// with fp16 operands and fp32 accumulation on the tensor cores (M=64, N=64,
+// K=64; issued by the MMA warp, results in TMEM columns 0-63, row 16 w + l in
+// lane 32 w + l).  The final X (fp32) replaces A in `am`.  Exact only when A^(2^(iters+1))
+// vanishes (iters >= 5 for C = 64); the fp16 operands bound its accuracy.
+// Called by NP = 256 threads (warp w: lane quarter w & 3, column half w >> 2).
+template <int NP>
+__device__ __forceinline__ bool ns_solve64(float* am, uint8_t* m16, uint8_t* x16, uint8_t* y16, uint32_t tmem,
+                                           uint64_t* nsr, uint64_t* nsd, int iters, volatile int* abort_flag) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  {
+    // M and X from A (rows rr, 16-byte chunks 2 cq, 2 cq + 1)
+    const int rr = tid >> 2, cq = tid & 3;
+    const float* arow = am + rr * kAStride;
+#pragma unroll
+    for (int c = 2 * cq; c < 2 * cq + 2; ++c) {
+      float mv[8], xv[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int m = 8 * c + e;
+        const float a = arow[m], d = (m == rr) ? 1.f : 0.f;
+        mv[e] = d + a;
+        xv[e] = d - a;
+      }
+      *reinterpret_cast<uint4*>(m16 + sw128_off(rr, c)) = pack8_f16(mv);
+      *reinterpret_cast<uint4*>(x16 + sw128_off(rr, c)) = pack8_f16(xv);
+    }
+  }
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(nsr);
+  const int lq = warp & 3, hc = warp >> 2;
+  const int t = 16 * lq + (lane & 15);
+  bool ok = true;
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      ok = mbar_wait_warp(nsd, h & 1, abort_flag);  // phase 2 it + h
+      if (bar_any(1, NP, !ok || *abort_flag)) return false;
+      tc_fence_after();
+      float x[32];
+      tmem_ld32w(tmem_addr(tmem, lq * 32, 32 * hc), x);
+      tc_fence_before();
+      const bool last = (h == 1) && (it + 1 == iters);
+      if (lane < 16) {
+        if (h == 0) {
+          // Y = 2I - M X
+#pragma unroll
+          for (int e = 0; e < 32; ++e) x[e] = ((32 * hc + e == t) ? 2.f : 0.f) - x[e];
+        }
+        if (last) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(am + t * kAStride + 32 * hc + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+        } else {
+          uint8_t* dst = h == 0 ? y16 : x16;
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(dst + sw128_off(t, 4 * hc + c)) = pack8_f16(x + 8 * c);
+        }
+      }
+      if (!last) {
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(nsr);
+      }
+    }
+  }
+  named_bar(1, NP);  // T visible in am to every thread
+  return ok;
 }
 
 // GDN_TRACE builds: clock64 at phase boundaries of CTAs 0-63 (24 slots each),
@@ -120,7 +195,8 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
 
   if (tid == 0) {
     for (int i = 0; i < wy::B_COUNT; ++i)
-      mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC || i == wy::B_NORM)
+      mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC || i == wy::B_NORM ||
+                           i == wy::B_NSR)
                               ? wy::kPrep / 32
                               : 1);
     *abort_flag = 0;
@@ -214,7 +290,27 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         mma_f16_ss_warp(tmem, sdesc(a, 16, 1024, kSw128), sdesc(a, 16, 1024, kSw128), id_s, kk > 0);
       }
       mma_commit_warp(&bars[wy::B_SFULL]);
-      ok = mbar_wait_warp(&bars[wy::B_TREADY], 0, abort_flag);
+      // Newton-Schulz solve (gdn_triton_v2.py:58-68): per iteration M X, then X (2I - M X),
+      // fp16 operands written by the prep warps: M at tw, X at tw + 8 KB, 2I - M X at zz
+      const int ns_iters = (P.flags >> GDN_FLAG_NS_ITERS_SHIFT) & 15;
+      if (P.flags & GDN_FLAG_SOLVER_NS) {
+        const uint32_t id_ns = idesc_f16(64, 64, 0, 0, 1);
+        for (int it = 0; it < ns_iters && ok; ++it) {
+#pragma unroll 1
+          for (int h = 0; h < 2 && ok; ++h) {
+            ok = mbar_wait_warp(&bars[wy::B_NSR], h & 1, abort_flag);  // phase 2 it + h
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t a = sb + wy::tw + (h ? 8192 : 0), b = sb + (h ? wy::zz : wy::tw + 8192);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_f16_ss_warp(tmem, sdesc(a + kk * 32, 16, 1024, kSw128), sdesc(b + kk * 2048, 8192, 1024, kSw128),
+                              id_ns, kk > 0);
+            mma_commit_warp(&bars[wy::B_NSD]);
+          }
+        }
+      }
+      ok = ok && mbar_wait_warp(&bars[wy::B_TREADY], 0, abort_flag);
     }
     if (ok) {
       // ([Tw_hi; Tb_hi] + [Tw_lo; Tb_lo]) [K | V] (M=128, N=256, K=64 twice):
@@ -351,7 +447,11 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       tc_fence_before();
       named_bar(1, NP);
       if (ptid == 0) WY_TR(3);
-      invert_unit_lower64<NP>(amat, ptid);  // T = (I + A)^-1 in place
+      if (P.flags & GDN_FLAG_SOLVER_NS)
+        ok = ns_solve64<NP>(amat, sm + wy::tw, sm + wy::tw + 8192, sm + wy::zz, tmem, &bars[wy::B_NSR],
+                            &bars[wy::B_NSD], (P.flags >> GDN_FLAG_NS_ITERS_SHIFT) & 15, abort_flag);
+      else
+        invert_unit_lower64<NP>(amat, ptid);  // T = (I + A)^-1 in place
       if (ptid == 0) WY_TR(4);
       // Tw = T diag(beta e^b), Tb = T diag(beta), each split hi + lo in the input dtype:
       // [Tw_hi; Tb_hi] and [Tw_lo; Tb_lo]

@@ -31,6 +31,8 @@ ERR_SCRATCH_LIMIT = 7
 FLAG_QK_L2NORM = 1
 FLAG_BETA_SIGMOID = 2
 FLAG_G_LOGSIGMOID = 4
+FLAG_SOLVER_NS = 8       # Newton-Schulz solve of (I + A)^-1 (gdn_triton_v2.py:58-68)
+NS_ITERS_SHIFT = 8       # its iteration count, 1..15, in bits 8-11
 
 # Scratch bytes of the two-kernel path per (batch, head, chunk of 64 steps);
 # gdn_fwd_workspace_bytes() is the authority, this mirrors it for sizing.

@@ -132,8 +132,14 @@ def _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status, scale=1
     return a
 
 
-def _prep_flags(use_qk_l2norm_in_kernel, beta_activation, g_activation):
+def _prep_flags(use_qk_l2norm_in_kernel, beta_activation, g_activation, solver="blocked", ns_iters=3):
     flags = 0
+    if solver == "newton_schulz":
+        if not 1 <= int(ns_iters) <= 15:
+            raise ValueError(f"ns_iters must be in 1..15 (got {ns_iters})")
+        flags |= _lib.FLAG_SOLVER_NS | (int(ns_iters) << _lib.NS_ITERS_SHIFT)
+    elif solver != "blocked":
+        raise ValueError(f"solver must be 'blocked' or 'newton_schulz' (got {solver!r})")
     if use_qk_l2norm_in_kernel:
         flags |= _lib.FLAG_QK_L2NORM
     if beta_activation is not None:
@@ -149,7 +155,8 @@ def _prep_flags(use_qk_l2norm_in_kernel, beta_activation, g_activation):
 
 def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output_dtype=None,
                   output_final_state=True, block_v=0, check=False, fused=False, scale=None,
-                  use_qk_l2norm_in_kernel=False, beta_activation=None, g_activation=None):
+                  use_qk_l2norm_in_kernel=False, beta_activation=None, g_activation=None, solver="blocked",
+                  ns_iters=3):
     """Chunked Gated DeltaNet forward on a B200.
 
     Args:
@@ -173,6 +180,9 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
             L2-normalised inside the kernel (gdn_ref.py:24-25), fp32 math
         beta_activation: 'sigmoid' if beta holds logits
         g_activation: 'logsigmoid' if g holds logits
+        solver: 'blocked' (exact fp32 inverse of I + A, the default) or
+            'newton_schulz' (the approximate fp16 iteration of
+            gdn_triton_v2.py:58-68, ``ns_iters`` steps; two-kernel path only)
     Returns:
         (o [B, T, H, V], h_final [B, H, V, K] fp32 or None)
 
@@ -181,7 +191,7 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
     gdn_triton.py:122-125.
     """
     B, T, H, K, V = _check_inputs(q, k, v, beta, g)
-    flags = _prep_flags(use_qk_l2norm_in_kernel, beta_activation, g_activation)
+    flags = _prep_flags(use_qk_l2norm_in_kernel, beta_activation, g_activation, solver, ns_iters)
     if g is None and g_activation is not None:
         raise ValueError("g_activation needs a g tensor")
     scale = 1.0 if scale is None else float(scale)
@@ -221,15 +231,16 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
     return o, ht
 
 
-def gdn_chunk_fwd_v2(q, k, v, beta, g, C=64, BV=32, num_warps=4, num_stages=1, iters=3, **kw):
+def gdn_chunk_fwd_v2(q, k, v, beta, g, C=64, BV=32, num_warps=4, num_stages=1, iters=3, solver="blocked", **kw):
     """Keyword-compatible stand-in for ``gdn_chunk_fwd_v2`` (gdn_triton_v2.py:92).
 
-    C and BV map to ``chunk_size`` and ``block_v``.  num_warps, num_stages and
-    iters tune the reference's Triton kernel and its Newton-Schulz solve; this
-    implementation inverts (I + A) exactly, so they have no effect.
+    C and BV map to ``chunk_size`` and ``block_v``; num_warps and num_stages
+    tune the reference's Triton kernel and have no counterpart.  The default
+    solver inverts (I + A) exactly; ``solver="newton_schulz"`` runs the
+    reference's iteration with ``iters`` steps instead (approximate).
     """
-    del num_warps, num_stages, iters
-    return gdn_chunk_fwd(q, k, v, beta, g, chunk_size=C, block_v=BV, **kw)
+    del num_warps, num_stages
+    return gdn_chunk_fwd(q, k, v, beta, g, chunk_size=C, block_v=BV, solver=solver, ns_iters=iters, **kw)
 
 
 def gdn_wy_prep(q, k, v, beta, g, chunk_size=64, check=True):
