@@ -163,12 +163,16 @@ __device__ __forceinline__ bool ns_solve64(float* am, uint8_t* m16, uint8_t* x16
   return ok;
 }
 
-// GDN_TRACE builds: clock64 at phase boundaries of CTAs 0-63 (24 slots each),
-// plus globaltimer at start / end and the SM id.
+// GDN_TRACE builds: clock64 at phase boundaries of CTAs GDN_TRACE_BASE ..
+// GDN_TRACE_BASE + 63 (24 slots each), plus globaltimer at start / end and the SM id.
 #ifdef GDN_TRACE
+#ifndef GDN_TRACE_BASE
+#define GDN_TRACE_BASE 0
+#endif
+#define WY_TRACED() (P.trace != nullptr && blockIdx.x - GDN_TRACE_BASE < 64u)
 #define WY_TR(slot)                                                                  \
   do {                                                                               \
-    if (P.trace != nullptr && blockIdx.x < 64) P.trace[blockIdx.x * 24 + (slot)] = clock64(); \
+    if (WY_TRACED()) P.trace[(blockIdx.x - GDN_TRACE_BASE) * 24 + (slot)] = clock64(); \
   } while (0)
 #else
 #define WY_TR(slot) \
@@ -211,13 +215,11 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
   const uint32_t tmem = *tmem_base_p;
   const uint32_t sb = smem_u32(sm);
 #ifdef GDN_TRACE
-  if (tid == 0 && P.trace != nullptr && blockIdx.x < 64) {
-    long long gt;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
+  if (tid == 0 && WY_TRACED()) {
     uint32_t smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    P.trace[blockIdx.x * 24 + 20] = gt;
-    P.trace[blockIdx.x * 24 + 22] = smid;
+    P.trace[(blockIdx.x - GDN_TRACE_BASE) * 24 + 20] = (long long)globaltimer();
+    P.trace[(blockIdx.x - GDN_TRACE_BASE) * 24 + 22] = smid;
   }
 #endif
   if (tid == 0) WY_TR(0);
@@ -670,11 +672,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     tmem_dealloc(tmem, 256);
     if (lane == 0) WY_TR(12);
 #ifdef GDN_TRACE
-    if (lane == 0 && P.trace != nullptr && blockIdx.x < 64) {
-      long long gt;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(gt));
-      P.trace[blockIdx.x * 24 + 21] = gt;
-    }
+    if (lane == 0 && WY_TRACED()) P.trace[(blockIdx.x - GDN_TRACE_BASE) * 24 + 21] = (long long)globaltimer();
 #endif
   }
 }
