@@ -76,8 +76,9 @@ static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
 // Packet pieces are staged in shared memory that the finished MMAs no longer
 // read and leave in bulk copies: Q' in place over q, o_intra over A/T,
 // N over [W | U_hi], c over [Kbar | U_lo].
+// B_FULL: k and q landed (all the S product needs); B_FULLV: v landed (first read by W U).
 enum { B_FULL = 0, B_SFULL, B_TREADY, B_WUFULL, B_EPA, B_PFULL, B_EPC, B_NCFULL, B_DONE, B_NORM, B_NSR, B_NSD,
-       B_COUNT };
+       B_FULLV, B_COUNT };
 }  // namespace wy
 
 __device__ __forceinline__ uint4 pack8_f16(const float* x) {
@@ -205,6 +206,16 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
                               : 1);
     *abort_flag = 0;
     fence_mbar_init();
+    // inputs first (before the TMEM allocation and the CTA barrier): k and q on
+    // B_FULL, v on B_FULLV, so that S = [K;Q] K^T does not wait for v
+    mbar_arrive_expect_tx(&bars[wy::B_FULL], 32768);
+    tma_load_4d(sm + wy::k0, &P.tm_k, &bars[wy::B_FULL], 0, t0, hh, bb);
+    tma_load_4d(sm + wy::q0, &P.tm_q, &bars[wy::B_FULL], 0, t0, hh, bb);
+    tma_load_4d(sm + wy::k1, &P.tm_k, &bars[wy::B_FULL], 64, t0, hh, bb);
+    tma_load_4d(sm + wy::q1, &P.tm_q, &bars[wy::B_FULL], 64, t0, hh, bb);
+    mbar_arrive_expect_tx(&bars[wy::B_FULLV], 16384);
+    tma_load_4d(sm + wy::v0, &P.tm_v, &bars[wy::B_FULLV], 0, t0, hh, bb);
+    tma_load_4d(sm + wy::v1, &P.tm_v, &bars[wy::B_FULLV], 64, t0, hh, bb);
   }
   if (warp == wy::kMmaWarp) {
     tmem_alloc(tmem_base_p, 256);
@@ -226,13 +237,6 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
 
   if (warp == wy::kMmaWarp) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(&bars[wy::B_FULL], 49152);
-      tma_load_4d(sm + wy::k0, &P.tm_k, &bars[wy::B_FULL], 0, t0, hh, bb);
-      tma_load_4d(sm + wy::q0, &P.tm_q, &bars[wy::B_FULL], 0, t0, hh, bb);
-      tma_load_4d(sm + wy::k1, &P.tm_k, &bars[wy::B_FULL], 64, t0, hh, bb);
-      tma_load_4d(sm + wy::q1, &P.tm_q, &bars[wy::B_FULL], 64, t0, hh, bb);
-      tma_load_4d(sm + wy::v0, &P.tm_v, &bars[wy::B_FULL], 0, t0, hh, bb);
-      tma_load_4d(sm + wy::v1, &P.tm_v, &bars[wy::B_FULL], 64, t0, hh, bb);
       // the CTA that most likely takes this one's place on the SM: its inputs into L2
       const int nb = blockIdx.x + P.pf_stride;
       if (P.pf_stride > 0 && nb < int(gridDim.x)) {
@@ -314,6 +318,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       }
       ok = ok && mbar_wait_warp(&bars[wy::B_TREADY], 0, abort_flag);
     }
+    ok = ok && mbar_wait_warp(&bars[wy::B_FULLV], 0, abort_flag);
     if (ok) {
       // ([Tw_hi; Tb_hi] + [Tw_lo; Tb_lo]) [K | V] (M=128, N=256, K=64 twice):
       // W = lanes 0-63 x cols 0-127, U = lanes 64-127 x cols 128-255.  Both T
@@ -625,6 +630,14 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         for (int c = 0; c < 4; ++c)
           *reinterpret_cast<uint4*>(dst + sw128_off(r, ((c0 & 63) >> 3) + c)) = pack8_f16(n + 8 * c);
       }
+      // N leaves while c is converted
+      fence_async_smem();
+      named_bar(1, NP);
+      if (ptid == 0) {
+        bulk_store(pkg + pkt::kN, sm + wy::tw, 16384);
+        bulk_store(pkg + pkt::kN + 16384, sm + wy::zz, 16384);
+        bulk_commit();
+      }
 #pragma unroll 1
       for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
         float cv[32];
@@ -638,8 +651,6 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       fence_async_smem();
       named_bar(1, NP);
       if (ptid == 0) {
-        bulk_store(pkg + pkt::kN, sm + wy::tw, 16384);
-        bulk_store(pkg + pkt::kN + 16384, sm + wy::zz, 16384);
         bulk_store(pkg + pkt::kCs, sm + wy::k0, 8192);
         bulk_store(pkg + pkt::kCs + 8192, sm + wy::k1, 8192);
         bulk_store(pkg + pkt::kCs + 16384, sm + wy::v0, 8192);
@@ -658,6 +669,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       // a failed wait: let the TMA loads land before the CTA releases its smem
       volatile int never = 0;
       mbar_wait(&bars[wy::B_FULL], 0, &never);
+      mbar_wait(&bars[wy::B_FULLV], 0, &never);
       if (P.status != nullptr) atomicOr(P.status, 1 << GDN_ERR_TIMEOUT);
     }
     __syncwarp();
