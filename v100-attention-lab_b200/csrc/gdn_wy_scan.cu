@@ -18,9 +18,9 @@
 //
 //   gdn_wy_kernel   chunk-parallel, one CTA per (b, h, chunk), two per SM:
 //                   S = [K;Q]K^T -> A, P; T in fp32; W, U (U split hi + lo);
-//                   then N, c, Q', o_intra on the tensor cores, written as a
-//                   96 KB packet of fp16 images in the exact shared-memory
-//                   layout the scan feeds to its tensor cores.
+//                   then N, c, Q', o_intra on the tensor cores, stored from
+//                   registers as a 96 KB packet of chunk-major fp16 images
+//                   that the scan feeds to its tensor cores as they are.
 //   gdn_scan_kernel one CTA per (b, h, 32-wide V slice), serial over chunks:
 //                   one 128x128x32 product per chunk on the critical path
 //                   (N S), plus Q' S off it; the state stays in registers.
@@ -39,13 +39,17 @@ namespace gdn {
 
 constexpr uint32_t kPacketBytes = uint32_t(kPacketBytesPerChunk);
 // packet layout (bytes)
+// Every piece is chunk-major: 16-byte chunk j (8 consecutive columns) of row r
+// sits at (j * rows + r) * 16.  The prep writes it straight from the TMEM-row
+// layout (a warp stores 32 consecutive rows of one chunk: 512 contiguous
+// bytes), and for N and Q' it is the no-swizzle K-major operand layout of the
+// scan's MMAs (8-row x 16-byte core matrices; next chunk = next K core matrix).
 namespace pkt {
-constexpr uint32_t kN = 0;        // N fp16, 128 x 128, K-major SW128: 2 column blocks of 16 KB
-constexpr uint32_t kQ = 32768;    // Q' fp16, 64 x 128, K-major SW128: 2 column blocks of 8 KB
+constexpr uint32_t kN = 0;        // N fp16, 128 x 128: 16 chunks x 128 rows
+constexpr uint32_t kQ = 32768;    // Q' fp16, 64 x 128: 16 chunks x 64 rows
 constexpr uint32_t kHdr = 49152;  // fp32 e^{b_C}
-constexpr uint32_t kHead = 49408; // [N | Q' | hdr]: one bulk copy
-constexpr uint32_t kCs = 49408;   // c fp16, 4 V slices x (128 rows x 64 B, SW64 rows)
-constexpr uint32_t kOs = 82176;   // o_intra fp16, 4 V slices x (64 rows x 64 B, SW64 rows)
+constexpr uint32_t kCs = 49408;   // c fp16, 4 V slices x (4 chunks x 128 rows)
+constexpr uint32_t kOs = 82176;   // o_intra fp16, 4 V slices x (4 chunks x 64 rows)
 static_assert(kOs + 4 * 4096 == kPacketBytesPerChunk, "packet size");
 }  // namespace pkt
 
@@ -63,7 +67,7 @@ constexpr uint32_t v0 = 32768, v1 = 49152;                     // later U_lo fp1
 constexpr uint32_t p16 = 40960;    // P fp16, 64 x 128 B
 constexpr uint32_t tw = 57344;     // [Tw_hi; Tb_hi] (input dtype): one M = 128 operand; later W fp16
 constexpr uint32_t zz = 73728;     // [Tw_lo; Tb_lo]: one M = 128 operand; later U_hi fp16
-constexpr uint32_t amat = 90112;   // fp32 A / T (64 x kAStride); later o_intra staging
+constexpr uint32_t amat = 90112;   // fp32 A / T (64 x kAStride)
 constexpr uint32_t vec = amat + 17408;  // kVecN x 64 fp32
 constexpr uint32_t bars = vec + kVecN * kC * 4;
 constexpr uint32_t misc = bars + 16 * 8;
@@ -73,9 +77,9 @@ static_assert(kC * kAStride * 4 <= 17408, "A/T region");
 static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
 // TMEM columns: S 0-63 (M=128); [W | Tw V ; Tb K | U] 0-255 (M=128: W = lanes 0-63 cols 0-127,
 // U = lanes 64-127 cols 128-255); PW 0-127, PU 128-255 (M=64); N 0-127, c 128-255 (M=128).
-// Packet pieces are staged in shared memory that the finished MMAs no longer
-// read and leave in bulk copies: Q' in place over q, o_intra over A/T,
-// N over [W | U_hi], c over [Kbar | U_lo].
+// Packet pieces go from registers straight to global memory (chunk-major, so
+// every warp store is 512 contiguous bytes): no staging, and nothing to drain
+// before the CTA leaves.
 // B_FULL: k and q landed (all the S product needs); B_FULLV: v landed (first read by W U).
 enum { B_FULL = 0, B_SFULL, B_TREADY, B_WUFULL, B_EPA, B_PFULL, B_EPC, B_NCFULL, B_DONE, B_NORM, B_NSR, B_NSD,
        B_FULLV, B_COUNT };
@@ -568,11 +572,10 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         float pw[32];
         tmem_ld32w(tmem_addr(tmem, lq * 32, c0), pw);
         if (lane < 16) {
-          uint8_t* qrow = sm + wy::q0 + (c0 >> 6) * 16384;
+          const uint8_t* qrow = sm + wy::q0 + (c0 >> 6) * 16384;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            uint4* pp = reinterpret_cast<uint4*>(qrow + sw128_off(t, ((c0 & 63) >> 3) + c));
-            const uint4 x = *pp;
+            const uint4 x = *reinterpret_cast<const uint4*>(qrow + sw128_off(t, ((c0 & 63) >> 3) + c));
             const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
             float y[8];
 #pragma unroll
@@ -581,7 +584,8 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
               y[2 * e] = fmaf(eb, f.x, -pw[8 * c + 2 * e]) * P.scale;
               y[2 * e + 1] = fmaf(eb, f.y, -pw[8 * c + 2 * e + 1]) * P.scale;
             }
-            *pp = pack8_f16(y);
+            const int j = (c0 >> 3) + c;  // 16-byte chunk of the 128 Q' columns
+            *reinterpret_cast<uint4*>(pkg + pkt::kQ + (j * 64 + t) * 16) = pack8_f16(y);
           }
         }
       }
@@ -590,28 +594,20 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         float ou[32];
         tmem_ld32w(tmem_addr(tmem, lq * 32, 128 + c0), ou);
         if (lane < 16) {
-          uint8_t* dst = sm + wy::amat + (c0 >> 5) * 4096;
+          uint8_t* dst = pkg + pkt::kOs + (c0 >> 5) * 4096;  // V slice c0 / 32
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             float sc8[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) sc8[e] = ou[8 * c + e] * P.scale;
-            *reinterpret_cast<uint4*>(dst + sw64_off(t, c)) = pack8_f16(sc8);
+            *reinterpret_cast<uint4*>(dst + (c * 64 + t) * 16) = pack8_f16(sc8);
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[wy::B_EPC]);
-      fence_async_smem();
-      named_bar(1, NP);
-      if (ptid == 0) {
-        bulk_store(pkg + pkt::kQ, sm + wy::q0, 8192);
-        bulk_store(pkg + pkt::kQ + 8192, sm + wy::q1, 8192);
-        bulk_store(pkg + pkt::kOs, sm + wy::amat, 16384);
-        bulk_commit();
-        WY_TR(11);
-      }
+      if (ptid == 0) WY_TR(11);
     }
     // ---- epilogue B: N = -(Kbar^T W) and c = Kbar^T U (row k1 = TMEM lane)
     ok = ok && mbar_wait_warp(&bars[wy::B_NCFULL], 0, abort_flag);
@@ -625,42 +621,24 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         tmem_ld32w(tmem_addr(tmem, lq * 32, c0), n);
 #pragma unroll
         for (int e = 0; e < 32; ++e) n[e] = -n[e];
-        uint8_t* dst = sm + (c0 < 64 ? wy::tw : wy::zz);
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(dst + sw128_off(r, ((c0 & 63) >> 3) + c)) = pack8_f16(n + 8 * c);
-      }
-      // N leaves while c is converted
-      fence_async_smem();
-      named_bar(1, NP);
-      if (ptid == 0) {
-        bulk_store(pkg + pkt::kN, sm + wy::tw, 16384);
-        bulk_store(pkg + pkt::kN + 16384, sm + wy::zz, 16384);
-        bulk_commit();
+        for (int c = 0; c < 4; ++c) {
+          const int j = (c0 >> 3) + c;  // 16-byte chunk of the 128 N columns
+          *reinterpret_cast<uint4*>(pkg + pkt::kN + (j * 128 + r) * 16) = pack8_f16(n + 8 * c);
+        }
       }
 #pragma unroll 1
       for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
         float cv[32];
         tmem_ld32w(tmem_addr(tmem, lq * 32, 128 + c0), cv);
-        uint8_t* dst = sm + wy::k0 + (c0 >> 5) * 16384;  // k0, k1, v0 (= U_lo 0), v1
+        uint8_t* dst = pkg + pkt::kCs + (c0 >> 5) * 8192;  // V slice c0 / 32
 #pragma unroll
-        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + sw64_off(r, c)) = pack8_f16(cv + 8 * c);
+        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + (c * 128 + r) * 16) = pack8_f16(cv + 8 * c);
       }
       if (ptid == 0) *reinterpret_cast<float*>(pkg + pkt::kHdr) = vec[V_EB * kC + kC - 1];
       tc_fence_before();
-      fence_async_smem();
-      named_bar(1, NP);
-      if (ptid == 0) {
-        bulk_store(pkg + pkt::kCs, sm + wy::k0, 8192);
-        bulk_store(pkg + pkt::kCs + 8192, sm + wy::k1, 8192);
-        bulk_store(pkg + pkt::kCs + 16384, sm + wy::v0, 8192);
-        bulk_store(pkg + pkt::kCs + 24576, sm + wy::v1, 8192);
-        bulk_commit();
-        WY_TR(9);
-      }
+      if (ptid == 0) WY_TR(9);
     }
-    // the bulk stores have read their shared-memory sources before the CTA goes away
-    if (ptid == 0) bulk_wait_read();
     if (!ok) *abort_flag = 1;
   }
   __syncthreads();
@@ -814,8 +792,7 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
       const uint32_t sbuf = sb + sc::s16 + (c % sc::kSBufs) * 8192;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss_warp(tmem + sc::kTmO + (c & 1) * BV,
-                        sdesc(st + sc::kOffQ + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024, kSw128),
+        mma_f16_ss_warp(tmem + sc::kTmO + (c & 1) * BV, sdesc(st + sc::kOffQ + kk * 2048, 1024, 128, kSwNone),
                         sdesc(sbuf + kk * 1024, 8192, 512, kSw64), id_o, kk > 0);
       mma_commit_warp(&bars[sc::B_DO + (c & 1)]);
       mma_commit_warp(&bars[sc::B_EMPTYB + s]);
@@ -834,7 +811,7 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
       const uint32_t sbuf = sb + sc::s16 + (c % sc::kSBufs) * 8192;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss_warp(tmem + sc::kTmN, sdesc(st + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024, kSw128),
+        mma_f16_ss_warp(tmem + sc::kTmN, sdesc(st + kk * 4096, 2048, 128, kSwNone),
                         sdesc(sbuf + kk * 1024, 8192, 512, kSw64), id_n, kk > 0);
       mma_commit_warp(&bars[sc::B_DN]);
       mma_commit_warp(&bars[sc::B_EMPTYA + s]);
@@ -877,7 +854,7 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
       if (lane < 16 && tg < P.T) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint4 x = *reinterpret_cast<const uint4*>(st + sc::kOffO + sw64_off(t, q));
+          const uint4 x = *reinterpret_cast<const uint4*>(st + sc::kOffO + (q * 64 + t) * 16);
           const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -906,7 +883,7 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
       float cv[BV];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint4 x = *reinterpret_cast<const uint4*>(st + sc::kOffC + sw64_off(r, q));
+        const uint4 x = *reinterpret_cast<const uint4*>(st + sc::kOffC + (q * 128 + r) * 16);
         const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
