@@ -803,7 +803,7 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
       const int s = c % sc::kStages;
       okm = mbar_wait_warp(&bars[sc::B_FULLA + s], (c / sc::kStages) & 1, abort_flag);
       if (lane == 0) GDN_TR(5, c);
-      okm = okm && mbar_wait_warp(&bars[sc::B_SREADY], c & 1, abort_flag);
+      okm = okm && mbar_spin_warp(&bars[sc::B_SREADY], c & 1, abort_flag);
       if (!okm) break;
       tc_fence_after();
       if (lane == 0) GDN_TR(1, c);
@@ -893,7 +893,7 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
         }
       }
       const float gam = *reinterpret_cast<const float*>(st + sc::kOffHdr);
-      ok = mbar_wait_warp(&bars[sc::B_DN], i & 1, abort_flag);
+      ok = mbar_spin_warp(&bars[sc::B_DN], i & 1, abort_flag);
       if (!ok) break;
       tc_fence_after();
       if (r == 0) GDN_TR(2, i);
