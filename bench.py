@@ -307,10 +307,20 @@ def run_ours(args, cfg, rank, world, local):
     with torch.cuda.graph(graph, stream=stream):
         for s in range(nsets):
             step(s)
-    reps = max(1, -(-args.steps // nsets))
-    steps = reps * nsets
+    # exactly K timed steps: K // nsets replays of the full rotation, then the
+    # first K % nsets input sets once more from a second graph
+    steps = max(1, args.steps)
+    reps, rem = divmod(steps, nsets)
+    graph_rem = None
+    if rem:
+        graph_rem = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_rem, stream=stream):
+            for s in range(rem):
+                step(s)
     for _ in range(max(3, -(-args.warmup // nsets))):
         graph.replay()
+    if graph_rem is not None:
+        graph_rem.replay()
     torch.cuda.synchronize(dev)
 
     clocks = ClockSampler(dev)
@@ -324,6 +334,8 @@ def run_ours(args, cfg, rank, world, local):
     e0.record(launch_stream)
     for _ in range(reps):
         graph.replay()
+    if graph_rem is not None:
+        graph_rem.replay()
     e1.record(launch_stream)
     torch.cuda.synchronize(dev)
     barrier(world)
