@@ -801,18 +801,23 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
     bool okm = true;
     for (int c = 0; c < NT && okm; ++c) {
       const int s = c % sc::kStages;
+      // descriptors first: after S' is ready only the issue itself remains
+      const uint32_t st = sb + sc::ringA + s * sc::kSlotA;
+      const uint32_t sbuf = sb + sc::s16 + (c % sc::kSBufs) * 8192;
+      uint64_t ad[8], bd[8];
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        ad[kk] = sdesc(st + kk * 4096, 2048, 128, kSwNone);
+        bd[kk] = sdesc(sbuf + kk * 1024, 8192, 512, kSw64);
+      }
       okm = mbar_wait_warp(&bars[sc::B_FULLA + s], (c / sc::kStages) & 1, abort_flag);
       if (lane == 0) GDN_TR(5, c);
       okm = okm && mbar_spin_warp(&bars[sc::B_SREADY], c & 1, abort_flag);
       if (!okm) break;
       tc_fence_after();
       if (lane == 0) GDN_TR(1, c);
-      const uint32_t st = sb + sc::ringA + s * sc::kSlotA;
-      const uint32_t sbuf = sb + sc::s16 + (c % sc::kSBufs) * 8192;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss_warp(tmem + sc::kTmN, sdesc(st + kk * 4096, 2048, 128, kSwNone),
-                        sdesc(sbuf + kk * 1024, 8192, 512, kSw64), id_n, kk > 0);
+      for (int kk = 0; kk < 8; ++kk) mma_f16_ss_warp(tmem + sc::kTmN, ad[kk], bd[kk], id_n, kk > 0);
       mma_commit_warp(&bars[sc::B_DN]);
       mma_commit_warp(&bars[sc::B_EMPTYA + s]);
       if (lane == 0) GDN_TR(6, c);
