@@ -161,7 +161,20 @@ def test_unsupported_requests_raise(gdn):
     with pytest.raises(NotImplementedError):
         gdn.gdn_chunk_fwd(qd.float(), kd.float(), vd.float(), bd, gd)
     with pytest.raises(NotImplementedError):
-        gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, chunk_size=32)
+        gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, chunk_size=16)
+
+
+def test_chunk_size_32_is_the_same_forward(gdn):
+    """The reference runs C = 32 and 64 (config 1; gdn_chunk_fwd_v2's default
+    is 32): both are the step recurrence, so both calls meet the oracle."""
+    qd, kd, vd, bd, gd, h0 = make(1, 200, 2, seed=36, dtype=torch.float16, h0_std=0.1)
+    o_ref, h_ref = oracle(qd, kd, vd, bd, gd, h0)
+    for C in (32, 64):
+        o, h = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, chunk_size=C, output_dtype=torch.float32,
+                                 check=True)
+        assert rel(o, o_ref) < TOL and rel(h, h_ref) < TOL
+    o, h = gdn.gdn_chunk_fwd_v2(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
+    assert rel(o, o_ref) < TOL and rel(h, h_ref) < TOL
 
 
 def test_repeat_calls_deterministic(gdn):

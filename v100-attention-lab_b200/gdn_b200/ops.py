@@ -166,7 +166,10 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
         g:    [B, T, H] log decay (<= 0), cast to fp32 if needed; None means
               g == 0 (no decay: the DeltaNet recurrence)
         initial_state: optional [B, H, V, K] state h0 (fp32 is used)
-        chunk_size: C (this build: 64)
+        chunk_size: C, 32 or 64 (the reference's two values).  C only sets
+            how the sequence is tiled: the forward is the step recurrence
+            for any C (gdn_ref.py:117-132 checks exactly that), so this build
+            computes with its 64-token chunks either way.
         output_dtype: dtype of o (default q.dtype, as gdn_triton.py:126)
         output_final_state: return the final state (else None)
         block_v: V columns per CTA (0 = choose)
@@ -191,6 +194,9 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
     gdn_triton.py:122-125.
     """
     B, T, H, K, V = _check_inputs(q, k, v, beta, g)
+    if chunk_size not in (32, 64):
+        raise NotImplementedError(f"chunk_size must be 32 or 64 (got {chunk_size})")
+    chunk_size = 64
     flags = _prep_flags(use_qk_l2norm_in_kernel, beta_activation, g_activation, solver, ns_iters)
     if g is None and g_activation is not None:
         raise ValueError("g_activation needs a g tensor")
@@ -231,11 +237,13 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
     return o, ht
 
 
-def gdn_chunk_fwd_v2(q, k, v, beta, g, C=64, BV=32, num_warps=4, num_stages=1, iters=3, solver="blocked", **kw):
-    """Keyword-compatible stand-in for ``gdn_chunk_fwd_v2`` (gdn_triton_v2.py:92).
+def gdn_chunk_fwd_v2(q, k, v, beta, g, C=32, BV=32, num_warps=4, num_stages=1, iters=3, solver="blocked", **kw):
+    """Keyword-compatible stand-in for ``gdn_chunk_fwd_v2`` (gdn_triton_v2.py:92),
+    with the reference's defaults.
 
-    C and BV map to ``chunk_size`` and ``block_v``; num_warps and num_stages
-    tune the reference's Triton kernel and have no counterpart.  The default
+    C maps to ``chunk_size`` (32 or 64; computed with 64-token chunks) and BV
+    to ``block_v``; num_warps and num_stages tune the reference's Triton
+    kernel and have no counterpart.  The default
     solver inverts (I + A) exactly; ``solver="newton_schulz"`` runs the
     reference's iteration with ``iters`` steps instead (approximate).
     """
