@@ -62,3 +62,15 @@ def test_v2_signature_is_keyword_compatible():
     assert params[:10] == ["q", "k", "v", "beta", "g", "C", "BV", "num_warps", "num_stages", "iters"]
     with pytest.raises(ValueError, match="CUDA"):
         gdn_b200.gdn_chunk_fwd_v2(*inputs(), C=64, BV=32, num_warps=4, num_stages=1, iters=2)
+
+
+def test_fixed_signature_matches_reference():
+    """gdn_chunk_fwd_fixed(q,k,v,beta,g,C=32,BV=32,num_warps=4,num_stages=1) (bench_gdn.py:43)."""
+    import inspect
+    sig = inspect.signature(gdn_b200.gdn_chunk_fwd_fixed)
+    params = list(sig.parameters)
+    assert params[:9] == ["q", "k", "v", "beta", "g", "C", "BV", "num_warps", "num_stages"]
+    assert sig.parameters["C"].default == 32 and sig.parameters["BV"].default == 32
+    assert inspect.signature(gdn_b200.gdn_chunk_fwd_v2).parameters["C"].default == 32
+    with pytest.raises(ValueError, match="CUDA"):
+        gdn_b200.gdn_chunk_fwd_fixed(*inputs())

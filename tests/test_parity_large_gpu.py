@@ -175,6 +175,9 @@ def test_chunk_size_32_is_the_same_forward(gdn):
         assert rel(o, o_ref) < TOL and rel(h, h_ref) < TOL
     o, h = gdn.gdn_chunk_fwd_v2(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
     assert rel(o, o_ref) < TOL and rel(h, h_ref) < TOL
+    # the reference's fixed-configuration launch (bench_gdn.py:43-59), same defaults
+    o, h = gdn.gdn_chunk_fwd_fixed(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
+    assert rel(o, o_ref) < TOL and rel(h, h_ref) < TOL
 
 
 def test_repeat_calls_deterministic(gdn):

@@ -251,6 +251,18 @@ def gdn_chunk_fwd_v2(q, k, v, beta, g, C=32, BV=32, num_warps=4, num_stages=1, i
     return gdn_chunk_fwd(q, k, v, beta, g, chunk_size=C, block_v=BV, solver=solver, ns_iters=iters, **kw)
 
 
+def gdn_chunk_fwd_fixed(q, k, v, beta, g, C=32, BV=32, num_warps=4, num_stages=1, **kw):
+    """Stand-in for ``gdn_chunk_fwd_fixed`` (bench_gdn.py:43-59): the forward
+    launched with a fixed configuration instead of the reference's autotuner.
+
+    Same arguments and outputs ``(o, hf)``; C and BV as in
+    ``gdn_chunk_fwd_v2``, num_warps / num_stages have no counterpart.  The
+    reference's fixed launch needs T to be a multiple of C; here any T works.
+    """
+    del num_warps, num_stages
+    return gdn_chunk_fwd(q, k, v, beta, g, chunk_size=C, block_v=BV, **kw)
+
+
 def gdn_wy_prep(q, k, v, beta, g, chunk_size=64, check=True):
     """The chunk-parallel WY/UT stage alone (gdn_ref.py:76-85).
 
