@@ -108,8 +108,8 @@ def test_fla_entry_layouts_and_default_scale(gdn):
     assert rel(o2, o_ref / math.sqrt(128)) < TOL + STORE_ROUNDING[BF16]
 
 
-def test_fla_entry_variable_lengths(gdn):
-    lens = [150, 77, 64]
+@pytest.mark.parametrize("lens", [[150, 77, 64], [96, 40, 96, 0, 40, 96]])
+def test_fla_entry_variable_lengths(gdn, lens):
     parts = [make(1, L, 2, seed=70 + i, dtype=BF16, h0_std=0.1) for i, L in enumerate(lens)]
     cat = lambda j: torch.cat([p[j] for p in parts], dim=1)
     q, k, v, b, g = (cat(j) for j in range(5))
@@ -119,6 +119,9 @@ def test_fla_entry_variable_lengths(gdn):
                                        cu_seqlens=cu, transpose_state_layout=True)
     s = 0
     for i, p in enumerate(parts):
+        if lens[i] == 0:  # an empty sequence keeps its state
+            assert torch.equal(ht[i], h0[i])
+            continue
         o_ref, h_ref = oracle(*p)
         assert rel(o[:, s:s + lens[i]], o_ref) < TOL + STORE_ROUNDING[BF16], i
         assert rel(ht[i:i + 1], h_ref) < TOL, i

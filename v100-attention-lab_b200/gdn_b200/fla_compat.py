@@ -13,8 +13,9 @@ they drop in where those are called:
 * states are ``[N, H, K, V]`` (FLA) unless ``transpose_state_layout=True``,
   which selects ``[N, H, V, K]``, the layout of gdn_ref / gdn_triton;
 * ``use_qk_l2norm_in_kernel`` normalises q and k rows inside the kernel;
-* ``cu_seqlens`` (variable-length batches, B = 1) runs one forward per
-  sequence on views of the packed tensors.
+* ``cu_seqlens`` (variable-length batches, B = 1) runs one batched forward
+  per distinct sequence length (equal-length sequences gathered into one
+  batch; a length that occurs once runs on views of the packed tensors).
 
 Forward only.  Grouped value heads (v with more heads than q), the in-kernel
 gate of newer FLA releases (``use_gate_in_kernel``) and context parallelism
@@ -85,19 +86,31 @@ def chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None, out
     H, V = q.shape[2], v.shape[-1]
     o = torch.zeros(q.shape[:3] + (V,), dtype=q.dtype, device=q.device)
     ht = torch.zeros(N, H, V, K, dtype=torch.float32, device=q.device) if output_final_state else None
+    # sequences of one length run as one batch (one forward per distinct length);
+    # a length that occurs once runs on views of the packed tensors, no copy
+    by_len = {}
     for i in range(N):
         s, e = int(bounds[i]), int(bounds[i + 1])
-        h0_i = None if h0 is None else h0[i:i + 1]
         if e <= s:  # empty sequence: the state passes through
-            if ht is not None and h0_i is not None:
-                ht[i] = h0_i[0]
+            if ht is not None and h0 is not None:
+                ht[i] = h0[i]
             continue
-        g_i = None if g is None else g[:, s:e]
-        o_i, ht_i = gdn_chunk_fwd(q[:, s:e], k[:, s:e], v[:, s:e], beta[:, s:e], g_i, initial_state=h0_i,
+        by_len.setdefault(e - s, []).append(i)
+    for L, idx in by_len.items():
+        starts = [int(bounds[i]) for i in idx]
+        if len(idx) == 1:
+            s = starts[0]
+            pick = lambda x: None if x is None else x[:, s:s + L]
+            h0_g = None if h0 is None else h0[idx[0]:idx[0] + 1]
+        else:
+            pick = lambda x: None if x is None else torch.cat([x[:, s:s + L] for s in starts], dim=0)
+            h0_g = None if h0 is None else h0[idx]
+        o_g, ht_g = gdn_chunk_fwd(pick(q), pick(k), pick(v), pick(beta), pick(g), initial_state=h0_g,
                                   output_final_state=output_final_state, **common)
-        o[:, s:e] = o_i
+        for j, s in enumerate(starts):
+            o[0, s:s + L] = o_g[j]
         if ht is not None:
-            ht[i] = ht_i[0]
+            ht[idx] = ht_g
     return o, _state_out(ht, transpose_state_layout)
 
 
