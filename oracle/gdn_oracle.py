@@ -30,6 +30,11 @@ It restates, in numpy, the two definitions of the reference's ``gdn_ref.py``
   ``h0 Wbar^T K`` term folds into ``u``.  The oracle keeps the reference's
   two-GEMM form in ``chunked(..., fold_state=False)`` so both are checked.
 
+* ``chunk_affine`` / ``scan_affine`` -- the same chunk written as an affine
+  map of its start state (the regrouping the B200 two-kernel path computes),
+  and a scan that composes two chunks per state step; both are pinned to
+  ``recurrent`` by the CPU tests.
+
 Layouts follow the reference: q, k [B, T, H, K]; v [B, T, H, V]; beta, g
 [B, T, H]; state [B, H, V, K] (K contiguous).  Padding follows
 ``pad_to_multiple`` (``gdn_ref.py:102-114``): padded steps carry q = k = v = 0,
@@ -45,7 +50,7 @@ from __future__ import annotations
 import numpy as np
 
 __all__ = ["l2norm", "recurrent", "chunked", "pad_to_multiple", "chunk_stages", "ns_inverse",
-           "make_inputs", "max_rel"]
+           "chunk_affine", "scan_affine", "make_inputs", "max_rel"]
 
 
 def l2norm(x: np.ndarray, eps: float = 1e-6) -> np.ndarray:
@@ -185,6 +190,68 @@ def chunked(q, k, v, beta, g, C=64, initial_state=None, dtype=np.float64,
             h = (np.einsum("bhvk,bhkl->bhvl", h, np.exp(bC)[..., None] * eyeK - WtK)
                  + np.einsum("bhcv,bhck->bhvk", Ub, kc))
     return o, h
+
+
+def chunk_affine(qc, kc, vc, bc, gc, dtype=np.float64):
+    """The chunk as an affine map of its start state S = h^T (K x V), the form
+    the two-kernel path computes (``gdn_ref.py:86-98`` regrouped):
+
+        S' = gamma S + N S + c          N = -Kbar^T W,  c = Kbar^T U
+        o  = Q' S + o_intra             Q' = Qhat - P W,  o_intra = P U
+
+    with Kbar = exp(b_C - b) k, Qhat = exp(b) q, P = tril(Q K^T * exp(b_t - b_j))
+    and gamma = exp(b_C).  Inputs per chunk as in ``chunk_stages``.
+    """
+    qc = qc.astype(dtype)
+    st = chunk_stages(kc, vc, bc, gc, dtype)
+    b, U, W, dec = st["b"], st["U"], st["W"], st["dec"]
+    kc = kc.astype(dtype)
+    bC = b[..., -1:]
+    kbar_t = np.swapaxes(kc * np.exp(bC - b)[..., None], -1, -2)
+    P = np.tril((qc @ np.swapaxes(kc, -1, -2)) * dec)
+    return {"gamma": np.exp(bC[..., 0]), "N": -(kbar_t @ W), "c": kbar_t @ U,
+            "Qp": qc * np.exp(b)[..., None] - P @ W, "o_intra": P @ U}
+
+
+def scan_affine(q, k, v, beta, g, C=64, initial_state=None, pairs=False, dtype=np.float64):
+    """Forward through ``chunk_affine``: one state step per chunk, or with
+    ``pairs`` one step per two chunks composed ahead of the scan:
+
+        N_pair = g2 N1 + g1 N2 + N2 N1     c_pair = g2 c1 + N2 c1 + c2
+        Q''_2  = g1 Q'_2 + Q'_2 N1         o''_2  = o_intra_2 + Q'_2 c1
+        S_next = g1 g2 S + N_pair S + c_pair,  o_1 = Q'_1 S + o_intra_1,  o_2 = Q''_2 S + o''_2
+
+    (M_i = g_i I + N_i; M2 M1 = g1 g2 I + N_pair).  T must be a multiple of C;
+    an odd number of chunks ends with a single step.  Returns (o, h_final).
+    """
+    q, k, v, beta, g = (_as(x, dtype) for x in (q, k, v, beta, g))
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    if T % C != 0:
+        raise ValueError(f"T={T} is not a multiple of C={C}; pad first")
+    nt = T // C
+    tr = lambda x: np.moveaxis(x.reshape((B, nt, C) + x.shape[2:]), 3, 1)  # [B,H,nt,C,...]
+    aff = chunk_affine(tr(q), tr(k), tr(v), tr(beta), tr(g), dtype)
+    S = (np.zeros((B, H, K, V), dtype=dtype) if initial_state is None
+         else np.swapaxes(_as(initial_state, dtype), -1, -2).copy())
+    o = np.empty((B, H, nt, C, V), dtype=dtype)
+    at = lambda name, i: aff[name][:, :, i]
+    i = 0
+    while i < nt:
+        if pairs and i + 1 < nt:
+            g1, g2 = at("gamma", i)[..., None, None], at("gamma", i + 1)[..., None, None]
+            N1, N2, c1, c2 = at("N", i), at("N", i + 1), at("c", i), at("c", i + 1)
+            Qp2 = at("Qp", i + 1)
+            o[:, :, i] = at("Qp", i) @ S + at("o_intra", i)
+            o[:, :, i + 1] = (g1 * Qp2 + Qp2 @ N1) @ S + at("o_intra", i + 1) + Qp2 @ c1
+            S = g1 * g2 * S + (g2 * N1 + g1 * N2 + N2 @ N1) @ S + (g2 * c1 + N2 @ c1 + c2)
+            i += 2
+        else:
+            o[:, :, i] = at("Qp", i) @ S + at("o_intra", i)
+            S = at("gamma", i)[..., None, None] * S + at("N", i) @ S + at("c", i)
+            i += 1
+    o = np.moveaxis(o, 1, 3).reshape(B, T, H, V)
+    return o, np.swapaxes(S, -1, -2)
 
 
 def pad_to_multiple(q, k, v, beta, g, C):

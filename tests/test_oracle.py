@@ -133,3 +133,14 @@ def test_newton_schulz_restatement():
     o_ex, _ = ora.chunked(q, k, v, b, g)
     o_ns, _ = ora.chunked(q, k, v, b, g, ns_iters=5)
     assert 0 < ora.max_rel(o_ns, o_ex) < 1e-3
+
+
+@pytest.mark.parametrize("pairs", [False, True])
+@pytest.mark.parametrize("T", [256, 192])  # 4 chunks; 3 chunks (a single step at the end)
+def test_affine_scan_equals_recurrence(pairs, T):
+    """The two-kernel path's regrouped per-chunk affine form, and the same with
+    two chunks composed per state step, are the step recurrence."""
+    q, k, v, b, g, h0 = ora.make_inputs(2, T, 2, 32, 24, seed=T + pairs, h0_std=0.3, key_corr=1.0)
+    o_r, h_r = ora.recurrent(q, k, v, b, g, initial_state=h0)
+    o_a, h_a = ora.scan_affine(q, k, v, b, g, C=64, initial_state=h0, pairs=pairs)
+    assert ora.max_rel(o_a, o_r) < 1e-10 and ora.max_rel(h_a, h_r) < 1e-10
