@@ -206,6 +206,30 @@ def test_newton_schulz_solver(gdn):
         gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, solver="newton_schulz", fused=True)
 
 
+@pytest.mark.parametrize("solver", ["blocked", "newton_schulz"])
+@pytest.mark.parametrize("in_dtype", [BF16, torch.float16])
+def test_input_prep_options_combined(gdn, solver, in_dtype):
+    """Every input-preparation option of one call at once (q/k L2 norm, beta
+    sigmoid, g logsigmoid, a q scale) with either solver: the prep applies them
+    in one pass over the chunk, so they are checked together as well as one by
+    one.  Five Newton-Schulz rounds are exact for C = 64 (A^64 = 0)."""
+    gen = torch.Generator().manual_seed(71)
+    B, T, H = 2, 390, 3
+    raw_q = (2.0 * torch.randn(B, T, H, 128, generator=gen)).to(in_dtype).cuda()
+    raw_k = (0.7 * torch.randn(B, T, H, 128, generator=gen)).to(in_dtype).cuda()
+    beta_logit = torch.randn(B, T, H, generator=gen).cuda()
+    g_logit = (torch.randn(B, T, H, generator=gen) + 1.0).cuda()
+    _, _, vd, _, _, h0 = make(B, T, H, seed=71, dtype=in_dtype, h0_std=0.1)
+    o, ht = gdn.gdn_chunk_fwd(raw_q, raw_k, vd, beta_logit, g_logit, initial_state=h0, check=True, scale=0.7,
+                              use_qk_l2norm_in_kernel=True, beta_activation="sigmoid", g_activation="logsigmoid",
+                              solver=solver, ns_iters=5)
+    assert o.dtype == in_dtype
+    o_ref, h_ref = oracle(_l2norm(raw_q), _l2norm(raw_k), vd, torch.sigmoid(beta_logit),
+                          torch.nn.functional.logsigmoid(g_logit), h0)
+    assert rel(o, 0.7 * o_ref) < TOL + STORE_ROUNDING[in_dtype]
+    assert rel(ht, h_ref) < TOL
+
+
 def test_sweep_harness(gdn):
     from gdn_b200 import sweep
     lines = sweep.run(config=1, reps=3, iters=(2,))

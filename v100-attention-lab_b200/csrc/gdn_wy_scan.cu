@@ -79,7 +79,9 @@ static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
 // U = lanes 64-127 cols 128-255); PW 0-127, PU 128-255 (M=64); N 0-127, c 128-255 (M=128).
 // Packet pieces go from registers straight to global memory (chunk-major, so
 // every warp store is 512 contiguous bytes): no staging, and nothing to drain
-// before the CTA leaves.
+// before the CTA leaves.  The stores carry an L2 evict-last policy so that as
+// many packets as fit are still in L2 when the scan reads them (the scan loads
+// its private c / o_intra slices evict-first); measured 1.3 % per forward.
 // B_FULL: k and q landed (all the S product needs); B_FULLV: v landed (first read by W U).
 enum { B_FULL = 0, B_SFULL, B_TREADY, B_WUFULL, B_EPA, B_PFULL, B_EPC, B_NCFULL, B_DONE, B_NORM, B_NSR, B_NSD,
        B_FULLV, B_COUNT };
@@ -567,6 +569,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       tc_fence_after();
       const int t = 16 * lq + (lane & 15);
       const float eb = vec[V_EB * kC + t];
+      const uint64_t keep = l2_policy_evict_last();  // packets: keep in L2 for the scan
 #pragma unroll 1
       for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
         float pw[32];
@@ -585,7 +588,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
               y[2 * e + 1] = fmaf(eb, f.y, -pw[8 * c + 2 * e + 1]) * P.scale;
             }
             const int j = (c0 >> 3) + c;  // 16-byte chunk of the 128 Q' columns
-            *reinterpret_cast<uint4*>(pkg + pkt::kQ + (j * 64 + t) * 16) = pack8_f16(y);
+            st_global_hint(pkg + pkt::kQ + (j * 64 + t) * 16, pack8_f16(y), keep);
           }
         }
       }
@@ -600,7 +603,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
             float sc8[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) sc8[e] = ou[8 * c + e] * P.scale;
-            *reinterpret_cast<uint4*>(dst + (c * 64 + t) * 16) = pack8_f16(sc8);
+            st_global_hint(dst + (c * 64 + t) * 16, pack8_f16(sc8), keep);
           }
         }
       }
@@ -615,6 +618,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     if (bar_any(1, NP, !ok || *abort_flag)) ok = false;
     if (ok) {
       tc_fence_after();
+      const uint64_t keep = l2_policy_evict_last();
 #pragma unroll 1
       for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
         float n[32];
@@ -624,7 +628,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int j = (c0 >> 3) + c;  // 16-byte chunk of the 128 N columns
-          *reinterpret_cast<uint4*>(pkg + pkt::kN + (j * 128 + r) * 16) = pack8_f16(n + 8 * c);
+          st_global_hint(pkg + pkt::kN + (j * 128 + r) * 16, pack8_f16(n + 8 * c), keep);
         }
       }
 #pragma unroll 1
@@ -633,7 +637,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         tmem_ld32w(tmem_addr(tmem, lq * 32, 128 + c0), cv);
         uint8_t* dst = pkg + pkt::kCs + (c0 >> 5) * 8192;  // V slice c0 / 32
 #pragma unroll
-        for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(dst + (c * 128 + r) * 16) = pack8_f16(cv + 8 * c);
+        for (int c = 0; c < 4; ++c) st_global_hint(dst + (c * 128 + r) * 16, pack8_f16(cv + 8 * c), keep);
       }
       if (ptid == 0) *reinterpret_cast<float*>(pkg + pkt::kHdr) = vec[V_EB * kC + kC - 1];
       tc_fence_before();
@@ -767,8 +771,10 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
           uint8_t* st = sm + sc::ringB + s * sc::kSlotB;
           mbar_arrive_expect_tx(fb, 16640 + 8192 + 4096);
           bulk_load(st + sc::kOffQ, pk + pkt::kQ, 16640, fb);
-          bulk_load(st + sc::kOffC, pk + pkt::kCs + slice * 8192, 8192, fb);
-          bulk_load(st + sc::kOffO, pk + pkt::kOs + slice * 4096, 4096, fb);
+          // this slice's c and o_intra are read by this CTA only: first out of L2
+          const uint64_t once = l2_policy_evict_first();
+          bulk_load_hint(st + sc::kOffC, pk + pkt::kCs + slice * 8192, 8192, fb, once);
+          bulk_load_hint(st + sc::kOffO, pk + pkt::kOs + slice * 4096, 4096, fb, once);
         }
       }
       issued = i + 1;
