@@ -83,6 +83,17 @@ def test_config3_long_sequence(gdn, T):
     check_pairs(o, ht, sampled_oracle(qd, kd, vd, bd, gd, None, pairs), pairs, TOL)
 
 
+@pytest.mark.parametrize("T", [150 * 64, 201 * 64 - 10])
+def test_prep_order_in_chunk_blocks(gdn, T):
+    """Segments of 128-255 chunks run the prep in 2 or 3 chunk blocks (the last
+    block first): every (head, chunk) is still computed once and lands in its
+    own packet.  150 chunks split evenly, 201 (ragged T) do not."""
+    qd, kd, vd, bd, gd, h0 = make(1, T, 2, seed=27, dtype=torch.bfloat16, h0_std=0.1)
+    o, ht = gdn.gdn_chunk_fwd(qd, kd, vd, bd, gd, initial_state=h0, output_dtype=torch.float32, check=True)
+    pairs = [(0, 0), (0, 1)]
+    check_pairs(o, ht, sampled_oracle(qd, kd, vd, bd, gd, h0, pairs), pairs, TOL)
+
+
 def test_config4_sampled_heads(gdn):
     """B8 T8192 H32 bf16 with h0: the sharded config run on one GPU, sampled pairs."""
     qd, kd, vd, bd, gd, h0 = make(8, 8192, 32, seed=24, dtype=torch.bfloat16, h0_std=0.1)

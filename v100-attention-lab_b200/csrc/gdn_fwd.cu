@@ -827,6 +827,10 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
     const int ns = (NT - c0 < ns_max) ? NT - c0 : ns_max;
     wp.c0 = sp.c0 = c0;
     wp.NS = sp.NS = ns;
+    // blocks of >= 64 chunks, at most 4 (measured: 4 blocks for 340-chunk
+    // segments, T = 65536; one block below 128 chunks, configs 2 and 4)
+    const int nblk = ns / 64 < 1 ? 1 : (ns / 64 > 4 ? 4 : ns / 64);
+    wp.blk_len = (ns + nblk - 1) / nblk;
     sp.h0 = (c0 == 0) ? a->h0 : state;
     int rc = run_wy(in_bf16, wp, a->B * a->H * ns, s);
     if (rc != GDN_OK) return rc;

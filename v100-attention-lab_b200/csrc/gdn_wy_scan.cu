@@ -187,7 +187,32 @@ __device__ __forceinline__ bool ns_solve64(float* am, uint8_t* m16, uint8_t* x16
   } while (0)
 #endif
 
-template <typename InT>
+// CTA order of the prep: the segment's chunks fall into blocks of P.blk_len
+// consecutive chunks, taken last block first, head-major inside a block (one
+// head's chunks run back to back, so its input rows and its packets are read and
+// written in address order).  The packets written last are the ones still in
+// L2 when the scan starts, and the scan starts at the segment's first chunks:
+// with several blocks those are the first block's packets instead of the last
+// heads' final chunks (T = 65536: 2.54 vs 2.60 ms per forward with 4 blocks).
+// One block (blk_len >= NS) is plain head-major order: the kernel's kBlocked =
+// false instantiation, which carries none of this code (its presence alone cost
+// 0.8 % at T = 4096).
+__device__ __forceinline__ void wy_cta_chunk(const WyParams& P, int x, int& il, int& bh) {
+  const int nbh = P.B * P.H;
+  for (int lo = (P.NS - 1) / P.blk_len * P.blk_len; lo >= 0; lo -= P.blk_len) {
+    const int n = min(P.NS - lo, P.blk_len);
+    if (x < nbh * n) {
+      bh = x / n;
+      il = lo + (x - bh * n);
+      return;
+    }
+    x -= nbh * n;
+  }
+  il = -1;  // past the grid
+  bh = 0;
+}
+
+template <typename InT, bool kBlocked>
 __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_constant__ WyParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -197,8 +222,13 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
   float* vec = reinterpret_cast<float*>(sm + wy::vec);
   float* amat = reinterpret_cast<float*>(sm + wy::amat);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int il = blockIdx.x % P.NS;      // chunk within the segment
-  const int bh = blockIdx.x / P.NS;
+  int il, bh;  // chunk within the segment, (batch, head)
+  if constexpr (kBlocked) {
+    wy_cta_chunk(P, blockIdx.x, il, bh);
+  } else {
+    il = blockIdx.x % P.NS;
+    bh = blockIdx.x / P.NS;
+  }
   const int hh = bh % P.H, bb = bh / P.H;
   const int chunk = P.c0 + il;
   const int t0 = chunk * kC;
@@ -246,7 +276,14 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       // the CTA that most likely takes this one's place on the SM: its inputs into L2
       const int nb = blockIdx.x + P.pf_stride;
       if (P.pf_stride > 0 && nb < int(gridDim.x)) {
-        const int nbh = nb / P.NS, nt0 = (P.c0 + nb % P.NS) * kC;
+        int nil, nbh;
+        if constexpr (kBlocked) {
+          wy_cta_chunk(P, nb, nil, nbh);
+        } else {
+          nil = nb % P.NS;
+          nbh = nb / P.NS;
+        }
+        const int nt0 = (P.c0 + nil) * kC;
         const int nhh = nbh % P.H, nbb = nbh / P.H;
         tma_prefetch_4d(&P.tm_k, 0, nt0, nhh, nbb);
         tma_prefetch_4d(&P.tm_k, 64, nt0, nhh, nbb);
@@ -940,9 +977,9 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
 }
 
 // ------------------------------------------------------------------ launchers
-template <typename InT>
+template <typename InT, bool kBlocked>
 int launch_wy(const WyParams& p, int grid, cudaStream_t s) {
-  auto kern = gdn_wy_kernel<InT>;
+  auto kern = gdn_wy_kernel<InT, kBlocked>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -971,7 +1008,9 @@ int launch_scan(const ScanParams& p, int grid, cudaStream_t s) {
 }
 
 int run_wy(int in_bf16, const WyParams& p, int grid, cudaStream_t s) {
-  return in_bf16 ? launch_wy<__nv_bfloat16>(p, grid, s) : launch_wy<__half>(p, grid, s);
+  if (p.blk_len < p.NS)
+    return in_bf16 ? launch_wy<__nv_bfloat16, true>(p, grid, s) : launch_wy<__half, true>(p, grid, s);
+  return in_bf16 ? launch_wy<__nv_bfloat16, false>(p, grid, s) : launch_wy<__half, false>(p, grid, s);
 }
 
 int run_scan(int out_dtype, const ScanParams& p, int grid, cudaStream_t s) {

@@ -21,6 +21,7 @@ struct WyParams {
   float scale;          // multiplies Q' and o_intra (q scaled)
   int flags;            // GDN_FLAG_*
   int pf_stride;        // CTAs resident at once (2 per SM): blockIdx + pf_stride is prefetched to L2
+  int blk_len;          // chunks per block of the CTA order (NS: one block): see wy_cta_chunk
 };
 
 // Serial scan over the packets of one segment.
