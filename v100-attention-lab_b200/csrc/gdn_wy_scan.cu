@@ -193,7 +193,7 @@ __device__ __forceinline__ bool ns_solve64(float* am, uint8_t* m16, uint8_t* x16
 // written in address order).  The packets written last are the ones still in
 // L2 when the scan starts, and the scan starts at the segment's first chunks:
 // with several blocks those are the first block's packets instead of the last
-// heads' final chunks (T = 65536: 2.54 vs 2.60 ms per forward with 4 blocks).
+// heads' final chunks (T = 65536: 2.54 vs 2.59 ms per forward with 4 blocks).
 // One block (blk_len >= NS) is plain head-major order: the kernel's kBlocked =
 // false instantiation, which carries none of this code (its presence alone cost
 // 0.8 % at T = 4096).
