@@ -2,29 +2,35 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 1|2|3|4]
 
-One JSON line on stdout (rank 0).  Metric: GDN fwd Mtokens/s (tokens = B*T)
-on BASELINE config 2 (B=2, T=4096, H=16, K=V=128, bf16, C=64, h0 ~ N(0, 0.1)).
+One JSON line on stdout (rank 0).  Metric: GDN fwd Mtokens/s (tokens = B*T).
+The default workload is the headline shape, config 2: B=2, T=4096, H=16,
+K=V=128, bf16 inputs, C=64, h0 ~ N(0, 0.1), fp32 state.
 
-* ``value``     device-resident throughput: inputs already in HBM, K launches
-                replayed from a CUDA graph, CUDA events around the K steps on
-                the launching stream, max over ranks.
+* ``value``     device-resident throughput: inputs already in HBM, K forwards
+                replayed from a CUDA graph, CUDA events around exactly K steps
+                on the launching stream, max over ranks.
+* ``eager``     the same K forwards as plain calls of ``gdn_chunk_fwd`` (no
+                graph): device time per step and the host time per call
+                (argument checks, ctypes, tensor maps, launches).
 * ``e2e``       the same metric through the public Python API with pinned host
                 buffers: every step copies its inputs host->device and reads o
                 and the final state back (copies of neighbouring steps overlap
                 on separate streams, as a streaming caller would run them).
 * ``roofline``  one forward (the prep kernel and the scan kernel it feeds):
-                its algorithmic bytes / its average device time (CUDA events
-                over the timed region), against the measured HBM copy
-                bandwidth; ``traffic`` is the DRAM bytes of both kernels per
-                forward from the committed ncu summary.
-* ``cpu_baseline`` the CPU oracle (numpy port of gdn_ref's chunked path) on the
-                host cores, rank 0 at N=1 only.
+                its algorithmic bytes / its average device time, against the
+                measured HBM copy bandwidth; ``traffic`` is the DRAM bytes of
+                both kernels per forward from the committed ncu summary.
+* ``cpu_baseline`` the reference's chunked CPU path (gdn_ref.gdn_chunk_ref,
+                restated in torch fp32 in oracle/gdn_chunk_torch.py) on the
+                host cores, full B*H, rank 0 at N=1 only.
 
-With N > 1 (torchrun), each rank owns a disjoint block of (batch, head)
-pairs of a global batch of 2*N sequences (weak scaling); the hot path has no
-collective.  ``--impl reference`` times the reference's CPU algorithm
-(the oracle port; the reference is pure Python and has no GPU path of its own
-to install here) on the same config and prints the same line.
+Multi-GPU (torchrun, one process per GPU): the (batch, head) pairs of one
+global input set are split by ``gdn_b200.shard.plan`` and each rank runs its
+shard through ``shard.local_inputs`` (views of the global tensors); the hot
+path has no collective.  Configs 1-3 scale weakly (the global batch is B*N,
+each rank owns the config's shape); config 4 (B8 T8192 H32) scales strongly
+(one global problem split N ways).  ``--impl reference`` times the
+reference's CPU path on the same config and prints the same line.
 """
 
 from __future__ import annotations
@@ -42,20 +48,20 @@ for _p in (os.path.join(ROOT, "v100-attention-lab_b200"), ROOT):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "GDN fwd Mtokens/s (B2 H16 K=V=128 T4096 bf16) + % of roofline"
 UNIT = "Mtokens/s"
 
 CONFIGS = {
-    1: dict(name="config1: B2 T2048 H8 K=V=128 fp16 C64 h0=0", B=2, T=2048, H=8, dtype="fp16", h0=False, gate_mean=0.0),
+    1: dict(name="config1: B2 T2048 H8 K=V=128 fp16 C64 h0=0", B=2, T=2048, H=8, dtype="fp16", h0=False,
+            gate_mean=0.0, scaling="weak"),
     2: dict(name="config2: B2 T4096 H16 K=V=128 bf16 C64 h0~N(0,0.1)", B=2, T=4096, H=16, dtype="bf16", h0=True,
-            gate_mean=0.0),
+            gate_mean=0.0, scaling="weak"),
     3: dict(name="config3: B2 T65536 H16 K=V=128 bf16 C64 g=logsigmoid(N(2,1))", B=2, T=65536, H=16, dtype="bf16",
-            h0=False, gate_mean=2.0),
-    4: dict(name="config4: B8 T8192 H32 K=V=128 bf16 C64 h0~N(0,0.1), (b,h) sharded", B=8, T=8192, H=32, dtype="bf16",
-            h0=True, gate_mean=0.0),
+            h0=False, gate_mean=2.0, scaling="weak"),
+    4: dict(name="config4: B8 T8192 H32 K=V=128 bf16 C64 h0~N(0,0.1), (b,h) sharded", B=8, T=8192, H=32,
+            dtype="bf16", h0=True, gate_mean=0.0, scaling="strong"),
 }
 K_DIM = V_DIM = 128
 CHUNK = 64
@@ -72,7 +78,7 @@ def load_peaks():
 
 
 def measured_traffic(config):
-    """DRAM bytes per launch from the committed ncu summary, if one covers this config."""
+    """DRAM bytes per forward from the committed ncu summary, if one covers this config."""
     path = os.path.join(ROOT, "profiles", f"gdn_fwd_config{config}_traffic.md")
     try:
         for line in open(path):
@@ -98,15 +104,18 @@ def algo_flops(B, T, H, C=CHUNK):
 
 
 # ----------------------------------------------------------------------------- inputs
-def make_inputs(cfg, B, seed, device, gen_device=None):
-    """Seeded synthetic inputs with the BASELINE distributions, generated on the GPU."""
+def make_inputs(cfg, B, seed, device):
+    """Seeded synthetic inputs with the workload's distributions: q, k
+    L2-normalised N(0,1) rows, v ~ N(0,1), beta = sigmoid(N(0,1)),
+    g = logsigmoid(N(gate_mean, 1)), h0 ~ N(0, 0.1) where the config has one.
+    Generated on ``device``; the same seed gives the same tensors on every GPU."""
     dt = torch.bfloat16 if cfg["dtype"] == "bf16" else torch.float16
     T, H = cfg["T"], cfg["H"]
     g = torch.Generator(device=device)
     g.manual_seed(seed)
 
     def l2n(x):
-        return (x / torch.sqrt((x * x).sum(-1, keepdim=True) + 1e-6))
+        return x / torch.sqrt((x * x).sum(-1, keepdim=True) + 1e-6)
 
     q = l2n(torch.randn(B, T, H, K_DIM, device=device, generator=g)).to(dt)
     k = l2n(torch.randn(B, T, H, K_DIM, device=device, generator=g)).to(dt)
@@ -117,9 +126,15 @@ def make_inputs(cfg, B, seed, device, gen_device=None):
     return q, k, v, beta, gg, h0
 
 
+def global_batch(cfg, world):
+    """Batch of the global problem: the config's own B for strong scaling,
+    B per rank for weak scaling."""
+    return cfg["B"] if cfg["scaling"] == "strong" else cfg["B"] * world
+
+
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons while the GPU is loaded."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -175,33 +190,55 @@ class ClockSampler:
                 if r[key].lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": rows[0]["smax"],
-                "reasons": sorted(reasons), "samples": len(loaded)}
+                "reasons": sorted(reasons), "samples": len(loaded),
+                "power_w_median": statistics.median(r["pw"] for r in loaded)}
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def cpu_baseline(cfg, budget_s=12.0):
-    """Time the numpy oracle (chunked UT path, fp32) on the host cores.
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    Sample: the config's shape restricted to a subset of (b, h) pairs, repeated
-    until ~budget_s of CPU work; throughput is scaled to the full B*H.
-    """
-    from oracle import gdn_oracle as ora
-    T, H, B = cfg["T"], cfg["H"], cfg["B"]
-    nbh = 2
-    q, k, v, beta, g, h0 = ora.make_inputs(1, T, nbh, K_DIM, V_DIM, seed=3, gate_mean=cfg["gate_mean"],
-                                           h0_std=0.1 if cfg["h0"] else None)
-    reps, t_tot = 0, 0.0
-    while t_tot < budget_s and reps < 50:
+
+def cpu_inputs(cfg, B, H, seed=3):
+    """CPU tensors of the workload's shape and distributions (bf16/fp16 q, k, v)."""
+    return make_inputs(dict(cfg, H=H), B, seed, torch.device("cpu"))
+
+
+def cpu_forward(cfg, B, H):
+    """One call of the reference's chunked path (torch fp32 restatement) on B x H pairs."""
+    from oracle.gdn_chunk_torch import chunked_fp32
+    q, k, v, beta, g, h0 = cpu_inputs(cfg, B, H)
+    T = cfg["T"]
+    assert T % CHUNK == 0
+
+    def run():
+        return chunked_fp32(q, k, v, beta, g, C=CHUNK, initial_state=h0)
+    return run
+
+
+def cpu_baseline(cfg, budget_s=15.0):
+    """Time the reference's chunked CPU path on the host cores: the full
+    workload (all B*H pairs) repeated until ~budget_s of CPU time, at least once."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, T, H = cfg["B"], cfg["T"], cfg["H"]
+    run = cpu_forward(cfg, B, H)
+    run()  # first call: thread pool and allocator warm-up, not timed
+    times = []
+    while not times or (sum(times) < budget_s and len(times) < 50):
         t0 = time.perf_counter()
-        ora.chunked(q, k, v, beta, g, C=CHUNK, initial_state=h0, dtype=np.float32)
-        t_tot += time.perf_counter() - t0
-        reps += 1
-    t_per_pair = t_tot / reps / nbh
-    tokens_per_s = (B * T) / (t_per_pair * B * H)
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return {"value": tokens_per_s / 1e6, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"numpy fp32 chunked oracle, T={T}, {nbh} (b,h) pairs x {reps} runs "
-                      f"({t_tot:.1f} s), scaled to B*H={B * H} pairs"}
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": B * T / t / 1e6, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "host_cpus": os.cpu_count(), "cpu_model": _cpu_model(),
+            "sample": f"gdn_chunk_ref (gdn_ref.py:48-99) restated in torch fp32, full workload B={B} T={T} H={H}, "
+                      f"median of {len(times)} runs ({sum(times):.1f} s), torch threads {torch.get_num_threads()}"}
 
 
 # ----------------------------------------------------------------------------- distributed
@@ -233,30 +270,48 @@ def barrier(world):
 
 
 # ----------------------------------------------------------------------------- arms
-def run_reference(args, cfg, rank, world):
+def run_reference(args, cfg, rank, world, budget_s=120.0):
+    """The reference's CPU path on rank 0 (other ranks exit without work).
+
+    Each step is one forward of the workload on the host cores; when K full
+    forwards would not fit in ~budget_s, each step is a bounded sample (the
+    first pairs of the workload), and tokens are counted for the pairs run."""
     if rank != 0:
         return None
-    res = []
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, T, H = cfg["B"], cfg["T"], cfg["H"]
+    steps = max(1, args.steps)
+    one = cpu_forward(cfg, 1, 1)
+    one()
+    t0 = time.perf_counter()
+    one()
+    t_pair = time.perf_counter() - t0
+    pairs = max(1, min(B * H, int(budget_s / steps / max(t_pair, 1e-6))))
+    sb, sh = (pairs // H, H) if pairs >= H else (1, pairs)
+    run = cpu_forward(cfg, sb, sh)
     for _ in range(args.warmup):
-        pass
-    samples = []
-    for _ in range(max(1, args.steps)):
-        cb = cpu_baseline(cfg, budget_s=max(2.0, 60.0 / max(1, args.steps)))
-        samples.append(cb["value"])
-        res.append(cb)
-    val = statistics.median(samples)
-    cb = dict(res[-1])
-    cb["value"] = val
-    line = {
+        run()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    val = sb * sh * T * steps / total / H / 1e6  # tokens of the full B*H workload per pair-set
+    sample = (f"gdn_chunk_ref (gdn_ref.py:48-99) restated in torch fp32; each step {sb}x{sh} of {B}x{H} "
+              f"(batch, head) pairs at T={T}, {steps} steps ({total:.1f} s), torch threads {torch.get_num_threads()}")
+    cb = {"value": val, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+          "host_cpus": os.cpu_count(), "cpu_model": _cpu_model(), "sample": sample}
+    return {
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
-        "config": {"workload": cfg["name"], "B": cfg["B"], "T": cfg["T"], "H": cfg["H"], "K": K_DIM, "V": V_DIM,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": total / steps * 1e3, "higher_is_better": True,
+        "scaling": cfg["scaling"], "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; the workload's distributions)",
+        "config": {"workload": cfg["name"], "B": B, "T": T, "H": H, "K": K_DIM, "V": V_DIM,
                    "chunk": CHUNK, "parallelism": "host cores"},
         "cpu_baseline": cb,
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    return line
 
 
 def launches_per_forward(B, T, H):
@@ -274,28 +329,37 @@ def launches_per_forward(B, T, H):
 
 def run_ours(args, cfg, rank, world, local):
     import gdn_b200
-    from gdn_b200 import _lib
+    from gdn_b200 import _lib, shard
     _lib.load()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    B_rank = cfg["B"] if world == 1 else cfg["B"]  # per-rank batch (weak scaling: global B = B * world)
     T, H = cfg["T"], cfg["H"]
-    in_bytes_one = B_rank * T * H * (2 * K_DIM + V_DIM) * 2
-    l2 = torch.cuda.get_device_properties(dev).L2_cache_size if hasattr(
-        torch.cuda.get_device_properties(dev), "L2_cache_size") else 126 * 2 ** 20
+    B_glob = global_batch(cfg, world)
+    plan = shard.plan(B_glob, H, world, rank)
+    # every rank builds the same global input sets from the global seeds and
+    # runs its own (batch, head) block of them: the product's sharding path
+    in_bytes_one = plan.pairs * T * (2 * K_DIM + V_DIM) * 2
+    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 * 2 ** 20)
     nsets = max(1, min(4, -(-2 * l2 // in_bytes_one)))  # rotate enough sets to exceed 2x L2
-    sets = [make_inputs(cfg, B_rank, seed=1000 * rank + s, device=dev) for s in range(nsets)]
+    sets = []
+    for s in range(nsets):
+        glob = make_inputs(cfg, B_glob, seed=1000 + s, device=dev)
+        sets.append(shard.local_inputs(plan, *glob))
+        del glob
+    torch.cuda.empty_cache()
+    B_rank = sets[0][0].shape[0]
+    H_rank = sets[0][0].shape[2]
     out_dtype = sets[0][0].dtype
 
     def step(s):
         q, k, v, beta, g, h0 = sets[s % nsets]
         return gdn_b200.gdn_chunk_fwd(q, k, v, beta, g, initial_state=h0, chunk_size=CHUNK)
 
-    # correctness guard on rank 0: one launch checked for kernel errors
+    # one launch checked for kernel errors before anything is timed
     step(0)
     gdn_b200.check_status(dev)
 
-    # CUDA graph holding one launch per input set; replayed K / nsets times
+    # CUDA graph holding one forward per input set, replayed K / nsets times
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(stream):
@@ -323,9 +387,16 @@ def run_ours(args, cfg, rank, world, local):
         graph_rem.replay()
     torch.cuda.synchronize(dev)
 
+    # clocks: sampled over a ~1.5 s soak of the same replays and the timed region
+    # right after it, so that the samples see the GPU under this load
     clocks = ClockSampler(dev)
     if rank == 0:
         clocks.start()
+    soak_end = time.perf_counter() + (1.5 if rank == 0 or world > 1 else 0.0)
+    while time.perf_counter() < soak_end:
+        for _ in range(20):
+            graph.replay()
+        torch.cuda.synchronize(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
     launch_stream = torch.cuda.current_stream(dev)
@@ -341,28 +412,48 @@ def run_ours(args, cfg, rank, world, local):
     barrier(world)
     if rank == 0:
         clocks.stop()
-    ms_local = e0.elapsed_time(e1)
-    ms = max_over_ranks(ms_local, world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
     gdn_b200.check_status(dev)
-    tokens_all = B_rank * T * world * steps
+    tokens_all = B_glob * T * steps
     value = tokens_all / (ms / 1e3) / 1e6
     ms_per_step = ms / steps
+
+    # eager: the same K forwards as plain calls on the current stream
+    with torch.cuda.stream(stream):
+        for s in range(3):
+            step(s)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    g0 = torch.cuda.Event(enable_timing=True)
+    g1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        g0.record(stream)
+        h0t = time.perf_counter()
+        for s in range(steps):
+            step(s)
+        host_s = time.perf_counter() - h0t
+        g1.record(stream)
+    torch.cuda.synchronize(dev)
+    eager_ms = max_over_ranks(g0.elapsed_time(g1), world)
+    host_us = max_over_ranks(host_s / steps * 1e6, world)
+    gdn_b200.check_status(dev)
 
     # e2e: public API with pinned host buffers, H2D of inputs and D2H of o + h_final every step
     host = []
     for s in range(min(nsets, 2)):
         host.append([None if x is None else x.cpu().pin_memory() for x in sets[s]])
-    e2e_steps = max(3, min(args.steps, 20))
+    e2e_steps = max(3, min(steps, 20))
     h2d = sum(x.numel() * x.element_size() for x in host[0] if x is not None)
-    o_host = torch.empty(B_rank, T, H, V_DIM, dtype=out_dtype).pin_memory()
-    ht_host = torch.empty(B_rank, H, V_DIM, K_DIM, dtype=torch.float32).pin_memory()
+    o_host = torch.empty(B_rank, T, H_rank, V_DIM, dtype=out_dtype).pin_memory()
+    ht_host = torch.empty(B_rank, H_rank, V_DIM, K_DIM, dtype=torch.float32).pin_memory()
     d2h = o_host.numel() * o_host.element_size() + ht_host.numel() * 4
 
     # Three streams so that PCIe works both ways at once: the inputs of step j+1
     # travel host->device while step j computes and step j-1's outputs travel
     # back; every step still copies its own inputs in and its results out.
     h2d_s, cmp_s, d2h_s = (torch.cuda.Stream(device=dev) for _ in range(3))
-    dbuf = [[None if x is None else torch.empty_like(x, device=dev) for x in host[0]] for _ in range(2)]
+    dbuf = [[None if x is None else torch.empty(x.shape, dtype=x.dtype, device=dev) for x in host[0]]
+            for _ in range(2)]
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_cmp = [torch.cuda.Event() for _ in range(2)]
 
@@ -397,30 +488,34 @@ def run_ours(args, cfg, rank, world, local):
     f1.record(d2h_s)
     torch.cuda.synchronize(dev)
     e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
-    e2e_value = B_rank * T * world * e2e_steps / (e2e_ms / 1e3) / 1e6
+    e2e_value = B_glob * T * e2e_steps / (e2e_ms / 1e3) / 1e6
 
     if rank != 0:
         return None
     hbm, tf, peak_src = load_peaks()
-    abytes = algo_bytes(B_rank, T, H, h0=cfg["h0"])
+    # roofline of one rank's forward (its shard), timed as the slowest rank's
+    abytes = algo_bytes(B_rank, T, H_rank, h0=cfg["h0"])
     kern_s = ms_per_step / 1e3
     achieved = abytes / kern_s / 1e9
-    flops = algo_flops(B_rank, T, H)
+    flops = algo_flops(B_rank, T, H_rank)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": cfg["dtype"], "data": "synthetic (seeded, BASELINE distributions)",
-        "config": {"workload": cfg["name"], "B_per_gpu": B_rank, "T": T, "H": H, "K": K_DIM, "V": V_DIM,
-                   "chunk": CHUNK, "global_B": B_rank * world,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": cfg["scaling"], "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": "synthetic (seeded; the workload's distributions)",
+        "config": {"workload": cfg["name"], "global_B": B_glob, "T": T, "H": H, "K": K_DIM, "V": V_DIM,
+                   "chunk": CHUNK, "per_gpu": f"B={B_rank} H={H_rank} ({plan.mode} shard of the global batch)",
                    "l2": f"inputs rotate over {nsets} resident sets ({nsets * in_bytes_one / 1e6:.0f} MB > 2x L2)",
-                   "parallelism": f"{world} GPU(s), disjoint (batch, head) shards, no collective"},
+                   "parallelism": f"{world} GPU(s), disjoint (batch, head) shards (gdn_b200.shard), "
+                                  f"no collective on the hot path"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": measured_traffic(args.config) if world == 1 else None,
                      "peak_source": peak_src, "algorithmic_bytes_per_launch": abytes,
                      "launch": "one forward = prep kernel + scan kernel",
                      "tensor_frac": flops / kern_s / 1e12 / tf},
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": steps * launches_per_forward(B_rank, T, H),
+        "eager": {"ms_per_step": eager_ms / steps, "value": tokens_all / (eager_ms / 1e3) / 1e6,
+                  "host_us_per_call": host_us},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+        "gpu_launches": steps * launches_per_forward(B_rank, T, H_rank),
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -431,7 +526,7 @@ def run_ours(args, cfg, rank, world, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))

@@ -151,9 +151,14 @@ uint64_t gdn_fwd_workspace_bytes(const gdn_fwd_args* args);
  *   operands plus one fp32 state per (batch, head)); larger requests return
  *   GDN_ERR_SCRATCH_LIMIT before any device work.  Longer sequences are run
  *   in as many segments of chunks as the array requires.
- * - The array is reserved on a device from the first call there (lazy
- *   module loading) until the process exits; that first call also looks up
- *   the array's device address, so make it before any stream capture.
+ * - Invalid or unsupported requests return the same codes as gdn_fwd_sm100,
+ *   checked before the size limit.
+ * - The array is reserved on a device from the library's first use there
+ *   (lazy module loading; with CUDA_MODULE_LOADING=EAGER, from context
+ *   creation) until the process exits.  The first call on a device looks up
+ *   the array's device address, so make it before any stream capture; the
+ *   address is cached, so the entry point must not be used after a
+ *   cudaDeviceReset or other reset of the device's primary context.
  * - All calls share the array: calls that may overlap on the GPU (other
  *   streams, other host threads on the same device) race and must be
  *   serialised by the caller.

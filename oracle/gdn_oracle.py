@@ -271,7 +271,7 @@ def pad_to_multiple(q, k, v, beta, g, C):
 
 
 def make_inputs(B, T, H, K, V, seed=0, gate_mean=0.0, h0_std=None, key_corr=0.0):
-    """Seeded synthetic float32 inputs with the BASELINE distributions.
+    """Seeded synthetic float32 inputs with the benchmark workloads' distributions.
 
     q, k = l2norm(N(0,1)) along K; v = N(0,1); beta = sigmoid(N(0,1));
     g = logsigmoid(N(gate_mean, 1)); h0 = N(0, h0_std) or None.

@@ -12,9 +12,9 @@ Fixtures
 selfcheck.npz   the reference's own CPU self-check case (gdn_ref.py:117-132):
                 torch seed 0, B2 T128 H3 K=V=64, beta~U(0.4,0.9), g~-U(0,0.1);
                 outputs of gdn_recurrent_ref and gdn_chunk_ref(C=32).
-cfg0.npz        BASELINE config 0: B1 T256 H2 K=V=64 fp32, h0 = 0, C=32, with
-                the BASELINE distributions (l2norm q/k, sigmoid beta,
-                logsigmoid g).
+cfg0.npz        config 0, the reference's CPU-runnable case: B1 T256 H2 K=V=64
+                fp32, h0 = 0, C=32, with the benchmark distributions
+                (l2norm q/k, sigmoid beta, logsigmoid g).
 h0_f16.npz      B1 T128 H2 K=V=128, fp16 q/k/v, random h0 (std 0.1); recurrent
                 (fp64) and chunked (C=64) outputs.
 bf16_ragged.npz B1 T100 H2 K=V=128, bf16 q/k/v, h0 = 0, T padded to 128 with
@@ -63,7 +63,7 @@ def main(ref_dir):
                             o_rec=_np(o1), h_rec=_np(h1), o_chunk=_np(o2), h_chunk=_np(h2),
                             C=np.int32(C))
 
-    # inputs with the BASELINE distributions, made with a seeded torch generator
+    # inputs with the benchmark distributions, made with a seeded torch generator
     def make(B, T, H, K, V, seed, dt, h0_std=None):
         gen = torch.Generator().manual_seed(seed)
         q = gdn_ref._l2norm(torch.randn(B, T, H, K, generator=gen)).to(dt)

@@ -37,3 +37,16 @@ def oracle(qd, kd, vd, bd, gd, h0d, chunked=False, C=64, ns_iters=None):
 
 def rel(x, ref):
     return ora.max_rel(x.float().cpu().numpy() if isinstance(x, torch.Tensor) else x, ref)
+
+
+def ulp_distance_16(a, b):
+    """Largest distance, in units in the last place, between two 16-bit float
+    tensors of the same dtype (sign-magnitude bit patterns mapped to ordered
+    integers, so -0 and +0 are 0 apart)."""
+    assert a.dtype == b.dtype and a.dtype in (torch.float16, torch.bfloat16)
+
+    def ordered(x):
+        i = x.contiguous().view(torch.int16).to(torch.int32)
+        return torch.where(i < 0, -32768 - i, i)  # negative: flip magnitude order
+
+    return int((ordered(a) - ordered(b)).abs().max().item())

@@ -1,4 +1,4 @@
-"""The bench's roofline model: algorithmic bytes/flops per BASELINE config."""
+"""The bench's roofline model: algorithmic bytes/flops per benchmark workload."""
 
 import bench
 

@@ -144,3 +144,27 @@ def test_affine_scan_equals_recurrence(pairs, T):
     o_r, h_r = ora.recurrent(q, k, v, b, g, initial_state=h0)
     o_a, h_a = ora.scan_affine(q, k, v, b, g, C=64, initial_state=h0, pairs=pairs)
     assert ora.max_rel(o_a, o_r) < 1e-10 and ora.max_rel(h_a, h_r) < 1e-10
+
+
+@pytest.mark.parametrize("name", ["selfcheck", "cfg0", "h0_f16", "stages"])
+def test_torch_chunked_restatement_matches_reference(name):
+    """The CPU baseline (oracle/gdn_chunk_torch.py, the reference's chunked
+    path restated in torch fp32) reproduces the reference's own chunked outputs."""
+    import torch
+    from oracle.gdn_chunk_torch import chunked_fp32
+    d = load(name)
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x))
+    h0 = t(d["h0"]) if "h0" in d else None
+    o, h = chunked_fp32(t(d["q"]), t(d["k"]), t(d["v"]), t(d["beta"]), t(d["g"]), C=int(d["C"]), initial_state=h0)
+    assert o.dtype == torch.float32 and h.dtype == torch.float32
+    assert ora.max_rel(o.numpy(), d["o_chunk"]) < 1e-5
+    assert ora.max_rel(h.numpy(), d["h_chunk"]) < 1e-5
+
+
+def test_torch_chunked_restatement_needs_whole_chunks():
+    import torch
+    from oracle.gdn_chunk_torch import chunked_fp32
+    x = torch.zeros(1, 100, 1, 64)
+    b = torch.zeros(1, 100, 1)
+    with pytest.raises(ValueError):
+        chunked_fp32(x, x, x, b, b, C=64)

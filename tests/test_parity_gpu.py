@@ -95,3 +95,33 @@ def test_segmented_workspace(gdn, cap_chunks, monkeypatch):
             assert rel(ht, h_ref) < TOL
         else:
             assert ht is None
+
+
+def test_two_streams_at_once(gdn):
+    """Forwards queued on two streams at the same time: each stream has its own
+    scratch, so the prep of one and the scan of the other may overlap on the
+    GPU without touching each other's packets.  Both match the oracle, and
+    equal (bit for bit) the same forwards run one after the other."""
+    from gdn_b200 import ops
+    a = make(1, 1000, 4, seed=61, dtype=torch.bfloat16, h0_std=0.1)
+    b = make(2, 640, 3, seed=62, dtype=torch.float16, h0_std=0.1)
+    seq = [gdn.gdn_chunk_fwd(*x[:5], initial_state=x[5], output_dtype=torch.float32, check=True) for x in (a, b)]
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    torch.cuda.synchronize()
+    res = []
+    for _ in range(4):  # several rounds, so that kernels of the two streams interleave
+        with torch.cuda.stream(s1):
+            ra = gdn.gdn_chunk_fwd(*a[:5], initial_state=a[5], output_dtype=torch.float32)
+        with torch.cuda.stream(s2):
+            rb = gdn.gdn_chunk_fwd(*b[:5], initial_state=b[5], output_dtype=torch.float32)
+        res.append((ra, rb))
+    torch.cuda.synchronize()
+    ops.check_status()
+    keys = [k for k in ops._workspaces if k[1] in (s1.cuda_stream, s2.cuda_stream)]
+    assert len(keys) == 2  # one scratch buffer per stream
+    for x, (o_seq, h_seq), k in ((a, seq[0], 0), (b, seq[1], 1)):
+        o_ref, h_ref = oracle(*x)
+        for r in res:
+            o, h = r[k]
+            assert torch.equal(o, o_seq) and torch.equal(h, h_seq)
+        assert rel(o_seq, o_ref) < TOL and rel(h_seq, h_ref) < TOL

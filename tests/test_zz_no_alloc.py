@@ -40,11 +40,20 @@ def _noalloc(env, q, k, v, beta, g, h0):
     return rc, o, ht
 
 
+def _sampled_oracle(qd, kd, vd, bd, gd, h0, pairs):
+    """fp64 step recurrence of the CPU oracle on single (batch, head) pairs."""
+    from gpu_util import oracle
+    sl = lambda x, b, h: x[b:b + 1, :, h:h + 1]
+    return [oracle(sl(qd, b, h), sl(kd, b, h), sl(vd, b, h), sl(bd, b, h), sl(gd, b, h),
+                   h0[b:b + 1, h:h + 1]) for b, h in pairs]
+
+
 def test_noalloc_matches_regular_entry_point_twice(env):
     from gpu_util import TOL, make, rel
     gdn, _lib, ops, _ = env
     # B*H = 32 heads and 32 chunks need ~103 MB of scratch in one piece, so
     # the 32 MiB array is used in four segments with the state carried over
+    pairs = [(0, 3), (1, 14)]
     for call, seed in enumerate((51, 52)):
         qd, kd, vd, bd, gd, h0 = make(2, 2048, 16, seed=seed, dtype=torch.bfloat16, h0_std=0.1)
         rc, o, ht = _noalloc(env, qd, kd, vd, bd, gd, h0)
@@ -54,6 +63,21 @@ def test_noalloc_matches_regular_entry_point_twice(env):
                                          output_dtype=torch.float32, check=True)
         assert rel(o, o_ref.cpu().numpy()) < TOL, call
         assert rel(ht, h_ref.cpu().numpy()) < TOL, call
+        # and against the CPU oracle itself, on two sampled (batch, head) pairs
+        for (b, h), (o_or, h_or) in zip(pairs, _sampled_oracle(qd, kd, vd, bd, gd, h0, pairs)):
+            assert rel(o[b:b + 1, :, h:h + 1], o_or) < TOL, (call, b, h)
+            assert rel(ht[b:b + 1, h:h + 1], h_or) < TOL, (call, b, h)
+
+
+def test_noalloc_reports_unsupported_shapes_before_the_size_limit(env):
+    """A shape this build does not handle (K = V = 64) is refused as
+    unsupported, even when B*H alone would also exceed the scratch."""
+    _, _lib, _, _ = env
+    for B, H in ((1, 2), (64, 32)):
+        q = torch.zeros(B, 64, H, 64, dtype=torch.bfloat16, device="cuda")
+        beta = torch.zeros(B, 64, H, device="cuda")
+        rc, _, _ = _noalloc(env, q, q.clone(), q.clone(), beta, beta.clone(), None)
+        assert rc == _lib.ERR_UNSUPPORTED, (B, H, _lib.status_string(rc))
 
 
 def test_noalloc_refuses_requests_beyond_its_scratch(env):

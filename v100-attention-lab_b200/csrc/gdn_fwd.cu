@@ -897,6 +897,10 @@ int run(const gdn_fwd_args* a, float* w_out, float* u_out, void* stream, bool pr
 }
 
 }  // namespace
+
+// Argument checks of gdn_fwd_sm100, for entry points that wrap it and must
+// report an invalid or unsupported request before their own checks.
+int validate_fwd_args(const gdn_fwd_args* a) { return validate(a, true); }
 }  // namespace gdn
 
 namespace gdn {

@@ -13,9 +13,14 @@
 //
 // The array (kScratchBytes = 32 MiB) lives in this file's device module.  With
 // the CUDA driver's default lazy module loading it is reserved on a device
-// when this entry point is first used there, and it stays reserved on that
-// device until the process exits.  Its device address is looked up once per
-// device, by the first call made with that device current.
+// when this library's device code is first used there (any of its entry
+// points); with CUDA_MODULE_LOADING=EAGER it is reserved when the context is
+// created, whether or not this entry point is ever called.  Either way it
+// stays reserved on that device until the process exits.  Its device address
+// is looked up once per device, by the first call made with that device
+// current, and cached for the life of the process: a cudaDeviceReset (or any
+// other reset of the primary context) invalidates the cached address, so this
+// entry point must not be used after one.
 //
 // Every call uses the same array and leaves the last call's data in it.  The
 // kernels never read a scratch byte that the same call has not written first,
@@ -62,8 +67,10 @@ int scratch_for_current_device(void** out) {
 }  // namespace gdn
 
 extern "C" int gdn_fwd_sm100_noalloc(const gdn_fwd_args* args, void* stream) {
-  if (args == nullptr || args->B < 1 || args->H < 1 || args->K < 1 || args->V < 1)
-    return GDN_ERR_INVALID_ARGUMENT;
+  // An invalid or unsupported request is reported as such, before the size
+  // check: a caller must not be told to shrink B*H when the shape is the problem.
+  const int vrc = gdn::validate_fwd_args(args);
+  if (vrc != GDN_OK) return vrc;
   // One chunk per (batch, head) must fit, next to one fp32 state per (b, h):
   // the sequence is then processed in as many segments as the array needs.
   const uint64_t pairs = uint64_t(args->B) * uint64_t(args->H);

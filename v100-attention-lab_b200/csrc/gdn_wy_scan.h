@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+#include "../../include/gdn_b200.h"
+
 namespace gdn {
 
 // Chunk-parallel prep: reads q, k, v (TMA, 64-column boxes, 128B swizzle),
@@ -40,6 +42,9 @@ struct ScanParams {
 constexpr uint64_t kPacketBytesPerChunk = 98560;
 
 int run_wy(int in_bf16, const WyParams& p, int grid, cudaStream_t s);
+// The argument checks of gdn_fwd_sm100 (a gdn_status code; GDN_OK if the
+// request is valid and supported).  Defined in gdn_fwd.cu.
+int validate_fwd_args(const ::gdn_fwd_args* a);
 int run_scan(int out_dtype, const ScanParams& p, int grid, cudaStream_t s);
 
 }  // namespace gdn

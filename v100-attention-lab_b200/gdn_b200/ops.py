@@ -33,21 +33,41 @@ class GdnError(RuntimeError):
 
 _DTYPES = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
 _status_words: dict[int, torch.Tensor] = {}
-_workspaces: dict[int, torch.Tensor] = {}
+# scratch of the two-kernel path, one per (device index, stream handle)
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
-# Upper bound of the per-device scratch of the two-kernel path; longer inputs
-# run in several segments of chunks, so memory does not grow with T.
+# Upper bound of the scratch of the two-kernel path per (device, stream);
+# longer inputs run in several segments of chunks, so memory does not grow
+# with T.
 WORKSPACE_CAP_BYTES = int(os.environ.get("GDN_B200_WORKSPACE_MB", "1024")) << 20
 
 
-def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Cached uint8 scratch on ``device``; grows (never shrinks) on demand."""
+def _workspace(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor:
+    """Cached uint8 scratch for launches on ``stream``; grows (never shrinks).
+
+    The packets of one forward live in this buffer from its prep kernel to its
+    scan kernel, so two forwards that may run at the same time must not share
+    it: each stream gets its own, and launches on one stream are ordered.  The
+    buffer is allocated while ``stream`` is current, so the caching allocator
+    ties it to that stream; a buffer that is replaced because it is too small
+    is freed in stream order behind the launches already queued on it.
+    """
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    w = _workspaces.get(idx)
+    key = (idx, int(stream.cuda_stream))
+    w = _workspaces.get(key)
     if w is None or w.numel() < nbytes:
-        w = torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
-        _workspaces[idx] = w
+        with torch.cuda.stream(stream):
+            w = torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _workspaces[key] = w
     return w
+
+
+def release_workspaces() -> None:
+    """Drop the cached scratch buffers (all devices and streams).
+
+    Forwards already queued keep their buffers alive until they complete (the
+    caching allocator frees each in its stream's order)."""
+    _workspaces.clear()
 
 
 def _status_word(device: torch.device) -> torch.Tensor:
@@ -192,6 +212,11 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
     T need not be a multiple of chunk_size: the tail is padded on the device
     with the rule of gdn_ref.py:102-114, without the host-side copies of
     gdn_triton.py:122-125.
+
+    Launches on the current stream of q's device (as the reference's Triton
+    launch does) and returns without synchronising.  The scratch of the
+    two-kernel path is cached per (device, stream), so forwards issued on
+    different streams may run at the same time.
     """
     B, T, H, K, V = _check_inputs(q, k, v, beta, g)
     if chunk_size not in (32, 64):
@@ -219,16 +244,16 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
     ht = torch.empty(B, H, V, K, dtype=torch.float32, device=dev) if output_final_state else None
     status = _status_word(dev)
     args = _fill_args(q, k, v, beta, g, h0, o, ht, chunk_size, block_v, status, scale, flags)
-    if not fused:
-        need = int(lib.gdn_fwd_workspace_bytes(ctypes.byref(args)))
-        per_head = B * H * (_lib.PACKET_BYTES_PER_CHUNK + V * K * 4)
-        nbytes = max(min(need, WORKSPACE_CAP_BYTES), per_head)
-        ws = _workspace(dev, nbytes)
-        args.workspace = ws.data_ptr()
-        args.workspace_bytes = ws.numel()
     with torch.cuda.device(dev):
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        rc = lib.gdn_fwd_sm100(ctypes.byref(args), ctypes.c_void_p(stream))
+        stream = torch.cuda.current_stream(dev)
+        if not fused:
+            need = int(lib.gdn_fwd_workspace_bytes(ctypes.byref(args)))
+            per_head = B * H * (_lib.PACKET_BYTES_PER_CHUNK + V * K * 4)
+            nbytes = max(min(need, WORKSPACE_CAP_BYTES), per_head)
+            ws = _workspace(dev, stream, nbytes)
+            args.workspace = ws.data_ptr()
+            args.workspace_bytes = ws.numel()
+        rc = lib.gdn_fwd_sm100(ctypes.byref(args), ctypes.c_void_p(stream.cuda_stream))
     if rc != _lib.OK:
         _raise(rc, "gdn_fwd_sm100")
     if check:
