@@ -811,11 +811,12 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
   wp.T = sp.T = a->T;
   wp.H = sp.H = a->H;
   sp.nslice = kV / BV;
+  int nsm = 0;
   {
-    int dev = 0, nsm = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess &&
-        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
-      wp.pf_stride = 2 * nsm;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || nsm < 1)
+      return GDN_ERR_CUDA;
   }
 #ifdef GDN_TRACE
   sp.trace = g_trace;
@@ -832,7 +833,7 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
     const int nblk = ns / 64 < 1 ? 1 : (ns / 64 > 4 ? 4 : ns / 64);
     wp.blk_len = (ns + nblk - 1) / nblk;
     sp.h0 = (c0 == 0) ? a->h0 : state;
-    int rc = run_wy(in_bf16, wp, a->B * a->H * ns, s);
+    int rc = run_wy(in_bf16, wp, nsm, s);
     if (rc != GDN_OK) return rc;
     rc = run_scan(a->out_dtype, sp, a->B * a->H * sp.nslice, s);
     if (rc != GDN_OK) return rc;

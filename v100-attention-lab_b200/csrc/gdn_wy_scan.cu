@@ -62,18 +62,24 @@ constexpr int kPrep = 256;
 constexpr int kMmaWarp = 8;
 // Column blocks of 64 elements (128-byte rows, 128B swizzle).  k0, k1, v0, v1
 // sit 16 KB apart so that [K | V] is one N = 256 MN-major operand.
-constexpr uint32_t k0 = 0, q0 = 8192, k1 = 16384, q1 = 24576;  // k later -> Kbar fp16 in place
+constexpr uint32_t k0 = 0, q0 = 8192, k1 = 16384, q1 = 24576;
 constexpr uint32_t v0 = 32768, v1 = 49152;                     // later U_lo fp16
 constexpr uint32_t p16 = 40960;    // P fp16, 64 x 128 B
 constexpr uint32_t tw = 57344;     // [Tw_hi; Tb_hi] (input dtype): one M = 128 operand; later W fp16
 constexpr uint32_t zz = 73728;     // [Tw_lo; Tb_lo]: one M = 128 operand; later U_hi fp16
-constexpr uint32_t amat = 90112;   // fp32 A / T (64 x kAStride)
-constexpr uint32_t vec = amat + 17408;  // kVecN x 64 fp32
-constexpr uint32_t bars = vec + kVecN * kC * 4;
+constexpr uint32_t amat = 90112;   // fp32 A / T (64 x kAStride); later Kbar fp16
+// Kbar = e^{b_C - b} k (fp16, two 64-column blocks, 128B swizzle) is written
+// over A / T, dead after the T split: k's own buffer is then free for the
+// next chunk's k as soon as epilogue A has read it.
+constexpr uint32_t kbar = amat;
+constexpr uint32_t vec = amat + 17408;  // 2 buffers (item parity) x kVecN x 64 fp32
+constexpr uint32_t kVecBytes = kVecN * kC * 4;
+constexpr uint32_t bars = vec + 2 * kVecBytes;
 constexpr uint32_t misc = bars + 16 * 8;
 constexpr uint32_t total = misc + 32;
 constexpr uint32_t alloc = total + 1024;
-static_assert(kC * kAStride * 4 <= 17408, "A/T region");
+static_assert(kC * kAStride * 4 <= 17408 && 2 * 8192 <= 17408, "A/T region");
+static_assert(amat % 1024 == 0, "Kbar tiles are 1024-byte aligned");
 static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
 // TMEM columns: S 0-63 (M=128); [W | Tw V ; Tb K | U] 0-255 (M=128: W = lanes 0-63 cols 0-127,
 // U = lanes 64-127 cols 128-255); PW 0-127, PU 128-255 (M=64); N 0-127, c 128-255 (M=128).
@@ -82,9 +88,39 @@ static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
 // before the CTA leaves.  The stores carry an L2 evict-last policy so that as
 // many packets as fit are still in L2 when the scan reads them (the scan loads
 // its private c / o_intra slices evict-first); measured 1.3 % per forward.
-// B_FULL: k and q landed (all the S product needs); B_FULLV: v landed (first read by W U).
-enum { B_FULL = 0, B_SFULL, B_TREADY, B_WUFULL, B_EPA, B_PFULL, B_EPC, B_NCFULL, B_DONE, B_NORM, B_NSR, B_NSD,
-       B_FULLV, B_COUNT };
+//
+// The kernel is persistent: CTA x takes the items (chunks) x, x + G, x + 2G, ...
+// of the grid's G CTAs, so the items in flight at any time are a contiguous
+// range, as with one CTA per item.  Each mbarrier completes one phase per item
+// (B_NSR / B_NSD an even number), so an item's phases have parity (item & 1).
+// The next item's inputs are loaded while this one finishes, each as soon as
+// its buffer is free: k after epilogue A (Kbar is out), q after epilogue C,
+// v (later U_lo) after the N / c products; its S product waits for epilogue B
+// to release TMEM.  Its g and beta are read into registers when this item
+// starts and its vectors are written (into the other of two buffers) while
+// the prep warps run this item's epilogues, so the next item's S product and
+// A / P phase wait for nothing but epilogue B (measured: vectors computed
+// after the N / c issue kept the prep warps idle ~7.8k of ~30k cycles per item).
+enum {
+  B_FULLK = 0,  // k landed
+  B_FULLQ,      // q landed
+  B_FULLV,      // v landed (first read by the W | U product)
+  B_VEC,        // the item's cumsum / beta vectors written (MMA warp)
+  B_SFULL,
+  B_TREADY,
+  B_WUFULL,
+  B_EPA,
+  B_PFULL,
+  B_EPC,
+  B_NCFULL,
+  B_EPB,        // epilogue B has read N and c: TMEM free for the next item
+  B_NORM,
+  B_NSR,
+  B_NSD,
+  B_DONE,
+  B_COUNT
+};
+static_assert(B_COUNT <= 16, "barrier region");
 }  // namespace wy
 
 __device__ __forceinline__ uint4 pack8_f16(const float* x) {
@@ -170,24 +206,7 @@ __device__ __forceinline__ bool ns_solve64(float* am, uint8_t* m16, uint8_t* x16
   return ok;
 }
 
-// GDN_TRACE builds: clock64 at phase boundaries of CTAs GDN_TRACE_BASE ..
-// GDN_TRACE_BASE + 63 (24 slots each), plus globaltimer at start / end and the SM id.
-#ifdef GDN_TRACE
-#ifndef GDN_TRACE_BASE
-#define GDN_TRACE_BASE 0
-#endif
-#define WY_TRACED() (P.trace != nullptr && blockIdx.x - GDN_TRACE_BASE < 64u)
-#define WY_TR(slot)                                                                  \
-  do {                                                                               \
-    if (WY_TRACED()) P.trace[(blockIdx.x - GDN_TRACE_BASE) * 24 + (slot)] = clock64(); \
-  } while (0)
-#else
-#define WY_TR(slot) \
-  do {              \
-  } while (0)
-#endif
-
-// CTA order of the prep: the segment's chunks fall into blocks of P.blk_len
+// Item order of the prep: the segment's chunks fall into blocks of P.blk_len
 // consecutive chunks, taken last block first, head-major inside a block (one
 // head's chunks run back to back, so its input rows and its packets are read and
 // written in address order).  The packets written last are the ones still in
@@ -197,7 +216,7 @@ __device__ __forceinline__ bool ns_solve64(float* am, uint8_t* m16, uint8_t* x16
 // One block (blk_len >= NS) is plain head-major order: the kernel's kBlocked =
 // false instantiation, which carries none of this code (its presence alone cost
 // 0.8 % at T = 4096).
-__device__ __forceinline__ void wy_cta_chunk(const WyParams& P, int x, int& il, int& bh) {
+__device__ __forceinline__ void wy_item_blocked(const WyParams& P, int x, int& il, int& bh) {
   const int nbh = P.B * P.H;
   for (int lo = (P.NS - 1) / P.blk_len * P.blk_len; lo >= 0; lo -= P.blk_len) {
     const int n = min(P.NS - lo, P.blk_len);
@@ -208,8 +227,62 @@ __device__ __forceinline__ void wy_cta_chunk(const WyParams& P, int x, int& il, 
     }
     x -= nbh * n;
   }
-  il = -1;  // past the grid
+  il = -1;  // past the last item
   bh = 0;
+}
+
+template <bool kBlocked>
+__device__ __forceinline__ void wy_item(const WyParams& P, int x, int& il, int& bh) {
+  if constexpr (kBlocked) {
+    wy_item_blocked(P, x, il, bh);
+  } else {
+    il = x % P.NS;
+    bh = x / P.NS;
+  }
+}
+
+// g and beta of steps t0 + lane and t0 + lane + 32 of head (bb, hh), as the
+// kernels use them (zero past T, gdn_ref.py:102-114; activations applied).
+struct WyStepVals {
+  float ga, gb, ba, bb;
+};
+__device__ __forceinline__ WyStepVals wy_step_vals(const WyParams& P, int bb, int hh, int t0, int lane) {
+  const float* gp = P.g == nullptr ? nullptr : P.g + bb * P.sg_b + hh * P.sg_h;
+  const float* bp = P.beta + bb * P.sb_b + hh * P.sb_h;
+  const int ta = t0 + lane, tb = t0 + lane + 32;
+  WyStepVals r;
+  r.ga = load_g(gp, (long long)ta * P.sg_t, ta < P.T, P.flags);
+  r.gb = load_g(gp, (long long)tb * P.sg_t, tb < P.T, P.flags);
+  r.ba = load_beta(bp, (long long)ta * P.sb_t, ta < P.T, P.flags);
+  r.bb = load_beta(bp, (long long)tb * P.sb_t, tb < P.T, P.flags);
+  return r;
+}
+
+// In-chunk cumsum of g (log2 units), beta, e^b and e^{b_C - b} of one chunk
+// into vec, from its WyStepVals.  Whole warp.
+__device__ __forceinline__ void wy_vectors(const WyStepVals& sv, float* vec, int lane) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  float xa = sv.ga * kLog2e;
+  float xb = sv.gb * kLog2e;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const float ya = __shfl_up_sync(0xffffffffu, xa, d);
+    const float yb = __shfl_up_sync(0xffffffffu, xb, d);
+    if (lane >= d) {
+      xa += ya;
+      xb += yb;
+    }
+  }
+  xb += __shfl_sync(0xffffffffu, xa, 31);
+  const float bC = __shfl_sync(0xffffffffu, xb, 31);
+  vec[V_B2 * kC + lane] = xa;
+  vec[V_B2 * kC + lane + 32] = xb;
+  vec[V_BETA * kC + lane] = sv.ba;
+  vec[V_BETA * kC + lane + 32] = sv.bb;
+  vec[V_EB * kC + lane] = fast_exp2(xa);
+  vec[V_EB * kC + lane + 32] = fast_exp2(xb);
+  vec[V_DD * kC + lane] = fast_exp2(bC - xa);
+  vec[V_DD * kC + lane + 32] = fast_exp2(bC - xb);
 }
 
 template <typename InT, bool kBlocked>
@@ -219,41 +292,22 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + wy::bars);
   uint32_t* tmem_base_p = reinterpret_cast<uint32_t*>(sm + wy::misc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + wy::misc + 4);
-  float* vec = reinterpret_cast<float*>(sm + wy::vec);
   float* amat = reinterpret_cast<float*>(sm + wy::amat);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int il, bh;  // chunk within the segment, (batch, head)
-  if constexpr (kBlocked) {
-    wy_cta_chunk(P, blockIdx.x, il, bh);
-  } else {
-    il = blockIdx.x % P.NS;
-    bh = blockIdx.x / P.NS;
-  }
-  const int hh = bh % P.H, bb = bh / P.H;
-  const int chunk = P.c0 + il;
-  const int t0 = chunk * kC;
-  uint8_t* const pkg = P.packets + (size_t(bh) * P.NS + il) * kPacketBytes;
+  const int G = int(gridDim.x);
+  const int nitems = P.B * P.H * P.NS;
+  const int my_n = int(blockIdx.x) < nitems ? (nitems - 1 - int(blockIdx.x)) / G + 1 : 0;
 
-  if (tid == 0) {
-    for (int i = 0; i < wy::B_COUNT; ++i)
-      mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC || i == wy::B_NORM ||
-                           i == wy::B_NSR)
-                              ? wy::kPrep / 32
-                              : 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-    // inputs first (before the TMEM allocation and the CTA barrier): k and q on
-    // B_FULL, v on B_FULLV, so that S = [K;Q] K^T does not wait for v
-    mbar_arrive_expect_tx(&bars[wy::B_FULL], 32768);
-    tma_load_4d(sm + wy::k0, &P.tm_k, &bars[wy::B_FULL], 0, t0, hh, bb);
-    tma_load_4d(sm + wy::q0, &P.tm_q, &bars[wy::B_FULL], 0, t0, hh, bb);
-    tma_load_4d(sm + wy::k1, &P.tm_k, &bars[wy::B_FULL], 64, t0, hh, bb);
-    tma_load_4d(sm + wy::q1, &P.tm_q, &bars[wy::B_FULL], 64, t0, hh, bb);
-    mbar_arrive_expect_tx(&bars[wy::B_FULLV], 16384);
-    tma_load_4d(sm + wy::v0, &P.tm_v, &bars[wy::B_FULLV], 0, t0, hh, bb);
-    tma_load_4d(sm + wy::v1, &P.tm_v, &bars[wy::B_FULLV], 64, t0, hh, bb);
-  }
   if (warp == wy::kMmaWarp) {
+    if (lane == 0) {
+      for (int i = 0; i < wy::B_COUNT; ++i)
+        mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC || i == wy::B_EPB ||
+                             i == wy::B_NORM || i == wy::B_NSR)
+                                ? wy::kPrep / 32
+                                : 1);
+      *abort_flag = 0;
+      fence_mbar_init();
+    }
     tmem_alloc(tmem_base_p, 256);
     tmem_relinquish();
   }
@@ -261,75 +315,73 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
   tc_fence_after();
   const uint32_t tmem = *tmem_base_p;
   const uint32_t sb = smem_u32(sm);
-#ifdef GDN_TRACE
-  if (tid == 0 && WY_TRACED()) {
-    uint32_t smid;
-    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    P.trace[(blockIdx.x - GDN_TRACE_BASE) * 24 + 20] = (long long)globaltimer();
-    P.trace[(blockIdx.x - GDN_TRACE_BASE) * 24 + 22] = smid;
-  }
-#endif
-  if (tid == 0) WY_TR(0);
-
-  if (warp == wy::kMmaWarp) {
-    if (lane == 0) {
-      // the CTA that most likely takes this one's place on the SM: its inputs into L2
-      const int nb = blockIdx.x + P.pf_stride;
-      if (P.pf_stride > 0 && nb < int(gridDim.x)) {
-        int nil, nbh;
-        if constexpr (kBlocked) {
-          wy_cta_chunk(P, nb, nil, nbh);
-        } else {
-          nil = nb % P.NS;
-          nbh = nb / P.NS;
-        }
-        const int nt0 = (P.c0 + nil) * kC;
-        const int nhh = nbh % P.H, nbb = nbh / P.H;
-        tma_prefetch_4d(&P.tm_k, 0, nt0, nhh, nbb);
-        tma_prefetch_4d(&P.tm_k, 64, nt0, nhh, nbb);
-        tma_prefetch_4d(&P.tm_q, 0, nt0, nhh, nbb);
-        tma_prefetch_4d(&P.tm_q, 64, nt0, nhh, nbb);
-        tma_prefetch_4d(&P.tm_v, 0, nt0, nhh, nbb);
-        tma_prefetch_4d(&P.tm_v, 64, nt0, nhh, nbb);
-      }
-    }
-    // in-chunk cumsum of g (log2 units) and beta; zero past T (gdn_ref.py:102-114)
-    constexpr float kLog2e = 1.4426950408889634f;
-    const float* gp = P.g == nullptr ? nullptr : P.g + bb * P.sg_b + hh * P.sg_h;
-    const float* bp = P.beta + bb * P.sb_b + hh * P.sb_h;
-    const int ta = t0 + lane, tb = t0 + lane + 32;
-    float xa = load_g(gp, (long long)ta * P.sg_t, ta < P.T, P.flags) * kLog2e;
-    float xb = load_g(gp, (long long)tb * P.sg_t, tb < P.T, P.flags) * kLog2e;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const float ya = __shfl_up_sync(0xffffffffu, xa, d);
-      const float yb = __shfl_up_sync(0xffffffffu, xb, d);
-      if (lane >= d) {
-        xa += ya;
-        xb += yb;
-      }
-    }
-    xb += __shfl_sync(0xffffffffu, xa, 31);
-    const float bC = __shfl_sync(0xffffffffu, xb, 31);
-    vec[V_B2 * kC + lane] = xa;
-    vec[V_B2 * kC + lane + 32] = xb;
-    vec[V_BETA * kC + lane] = load_beta(bp, (long long)ta * P.sb_t, ta < P.T, P.flags);
-    vec[V_BETA * kC + lane + 32] = load_beta(bp, (long long)tb * P.sb_t, tb < P.T, P.flags);
-    vec[V_EB * kC + lane] = fast_exp2(xa);
-    vec[V_EB * kC + lane + 32] = fast_exp2(xb);
-    vec[V_DD * kC + lane] = fast_exp2(bC - xa);
-    vec[V_DD * kC + lane + 32] = fast_exp2(bC - xb);
-  }
-  __syncthreads();  // vec visible
-
   constexpr uint32_t kInBf16 = Cvt<InT>::kIsBf16;
-  bool ok = true;
+
   if (warp == wy::kMmaWarp) {
-    // ------------------------------------------------ MMA issue (the whole warp; elect.sync inside)
-    ok = mbar_wait_warp(&bars[wy::B_FULL], 0, abort_flag);
-    if (P.flags & GDN_FLAG_QK_L2NORM) ok = ok && mbar_wait_warp(&bars[wy::B_NORM], 0, abort_flag);
-    if (lane == 0) WY_TR(1);
-    if (ok) {
+    // ------------------------------------------------ TMA, vectors and MMA issue (the whole warp; elect.sync inside)
+    float* vec_buf = reinterpret_cast<float*>(sm + wy::vec);
+    uint32_t nk = 0, nq = 0, nv = 0;  // loads issued on B_FULLK / B_FULLQ / B_FULLV
+    auto load_k = [&](int t0, int hh, int bb) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars[wy::B_FULLK], 16384);
+        tma_load_4d(sm + wy::k0, &P.tm_k, &bars[wy::B_FULLK], 0, t0, hh, bb);
+        tma_load_4d(sm + wy::k1, &P.tm_k, &bars[wy::B_FULLK], 64, t0, hh, bb);
+      }
+      ++nk;
+    };
+    auto load_q = [&](int t0, int hh, int bb) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars[wy::B_FULLQ], 16384);
+        tma_load_4d(sm + wy::q0, &P.tm_q, &bars[wy::B_FULLQ], 0, t0, hh, bb);
+        tma_load_4d(sm + wy::q1, &P.tm_q, &bars[wy::B_FULLQ], 64, t0, hh, bb);
+      }
+      ++nq;
+    };
+    auto load_v = [&](int t0, int hh, int bb) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars[wy::B_FULLV], 16384);
+        tma_load_4d(sm + wy::v0, &P.tm_v, &bars[wy::B_FULLV], 0, t0, hh, bb);
+        tma_load_4d(sm + wy::v1, &P.tm_v, &bars[wy::B_FULLV], 64, t0, hh, bb);
+      }
+      ++nv;
+    };
+    bool ok = true;
+    if (my_n > 0) {
+      int il, bh;
+      wy_item<kBlocked>(P, blockIdx.x, il, bh);
+      const int t0 = (P.c0 + il) * kC, hh = bh % P.H, bb = bh / P.H;
+      load_k(t0, hh, bb);
+      load_q(t0, hh, bb);
+      load_v(t0, hh, bb);
+      wy_vectors(wy_step_vals(P, bb, hh, t0, lane), vec_buf, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[wy::B_VEC]);
+    }
+    for (int it = 0; it < my_n && ok; ++it) {
+      const uint32_t ph = uint32_t(it) & 1u;
+      const bool has_next = it + 1 < my_n;
+      int nt0 = 0, nhh = 0, nbb = 0;
+      WyStepVals nsv = {0.f, 0.f, 0.f, 0.f};
+      if (has_next) {
+        int nil, nbh;
+        wy_item<kBlocked>(P, int(blockIdx.x) + (it + 1) * G, nil, nbh);
+        nt0 = (P.c0 + nil) * kC;
+        nhh = nbh % P.H;
+        nbb = nbh / P.H;
+        if (lane == 0) {  // the next item's inputs into L2 now; its loads start during this item
+          tma_prefetch_4d(&P.tm_k, 0, nt0, nhh, nbb);
+          tma_prefetch_4d(&P.tm_k, 64, nt0, nhh, nbb);
+          tma_prefetch_4d(&P.tm_q, 0, nt0, nhh, nbb);
+          tma_prefetch_4d(&P.tm_q, 64, nt0, nhh, nbb);
+          tma_prefetch_4d(&P.tm_v, 0, nt0, nhh, nbb);
+          tma_prefetch_4d(&P.tm_v, 64, nt0, nhh, nbb);
+        }
+        nsv = wy_step_vals(P, nbb, nhh, nt0, lane);  // used after the W | U issue
+      }
+      ok = mbar_wait_warp(&bars[wy::B_FULLK], ph, abort_flag) && mbar_wait_warp(&bars[wy::B_FULLQ], ph, abort_flag);
+      if (P.flags & GDN_FLAG_QK_L2NORM) ok = ok && mbar_wait_warp(&bars[wy::B_NORM], ph, abort_flag);
+      if (it > 0) ok = ok && mbar_wait_warp(&bars[wy::B_EPB], ph ^ 1u, abort_flag);  // TMEM released
+      if (!ok) break;
       // S = [K;Q] K^T: M=128 (k rows then q rows), N=64, K=128
       tc_fence_after();
       const uint32_t id_s = idesc_f16(128, 64, kInBf16, 0, 0);
@@ -344,10 +396,10 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       const int ns_iters = (P.flags >> GDN_FLAG_NS_ITERS_SHIFT) & 15;
       if (P.flags & GDN_FLAG_SOLVER_NS) {
         const uint32_t id_ns = idesc_f16(64, 64, 0, 0, 1);
-        for (int it = 0; it < ns_iters && ok; ++it) {
+        for (int nit = 0; nit < ns_iters && ok; ++nit) {
 #pragma unroll 1
           for (int h = 0; h < 2 && ok; ++h) {
-            ok = mbar_wait_warp(&bars[wy::B_NSR], h & 1, abort_flag);  // phase 2 it + h
+            ok = mbar_wait_warp(&bars[wy::B_NSR], h & 1, abort_flag);  // phase 2 nit + h
             if (!ok) break;
             tc_fence_after();
             const uint32_t a = sb + wy::tw + (h ? 8192 : 0), b = sb + (h ? wy::zz : wy::tw + 8192);
@@ -359,10 +411,9 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
           }
         }
       }
-      ok = ok && mbar_wait_warp(&bars[wy::B_TREADY], 0, abort_flag);
-    }
-    ok = ok && mbar_wait_warp(&bars[wy::B_FULLV], 0, abort_flag);
-    if (ok) {
+      ok = ok && mbar_wait_warp(&bars[wy::B_TREADY], ph, abort_flag) &&
+           mbar_wait_warp(&bars[wy::B_FULLV], ph, abort_flag);
+      if (!ok) break;
       // ([Tw_hi; Tb_hi] + [Tw_lo; Tb_lo]) [K | V] (M=128, N=256, K=64 twice):
       // W = lanes 0-63 x cols 0-127, U = lanes 64-127 x cols 128-255.  Both T
       // operands are split hi + lo in the input dtype: with bf16 inputs one
@@ -375,9 +426,17 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         mma_f16_ss_warp(tmem, sdesc(sb + (kk < 4 ? wy::tw : wy::zz) + (kk & 3) * 32, 16, 1024, kSw128),
                         sdesc(sb + wy::k0 + (kk & 3) * 2048, 16384, 1024, kSw128), id_wu, kk > 0);
       mma_commit_warp(&bars[wy::B_WUFULL]);
-      ok = mbar_wait_warp(&bars[wy::B_EPA], 0, abort_flag);
-    }
-    if (ok) {
+      if (has_next) {
+        // the next item's vectors into the other buffer: every prep warp has
+        // passed this item's B_VEC wait (they arrived on B_TREADY), and that
+        // buffer's previous item read it for the last time in its epilogue C
+        wy_vectors(nsv, vec_buf + (ph ^ 1u) * (wy::kVecBytes / 4), lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[wy::B_VEC]);
+      }
+      ok = mbar_wait_warp(&bars[wy::B_EPA], ph, abort_flag);
+      if (!ok) break;
+      if (has_next) load_k(nt0, nhh, nbb);  // epilogue A has read k and written Kbar elsewhere
       // P W -> cols 0-127, P (U_hi + U_lo) -> cols 128-255  (M=64, N=128, K=64; B MN-major)
       tc_fence_after();
       const uint32_t id_p = idesc_f16(64, 128, 0, 0, 1);
@@ -392,305 +451,318 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
                                : sdesc(sb + wy::v0 + (kk & 3) * 2048, 16384, 1024, kSw128),
                         id_p, kk > 0);
       mma_commit_warp(&bars[wy::B_PFULL]);
-      ok = mbar_wait_warp(&bars[wy::B_EPC], 0, abort_flag);
-    }
-    if (ok) {
+      ok = mbar_wait_warp(&bars[wy::B_EPC], ph, abort_flag);
+      if (!ok) break;
       // Kbar^T W -> cols 0-127, Kbar^T (U_hi + U_lo) -> cols 128-255  (M=128, N=128, K=64; A and B MN-major)
       tc_fence_after();
       const uint32_t id_n = idesc_f16(128, 128, 0, 1, 1);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
-        mma_f16_ss_warp(tmem, sdesc(sb + wy::k0 + kk * 2048, 16384, 1024, kSw128),
+        mma_f16_ss_warp(tmem, sdesc(sb + wy::kbar + kk * 2048, 8192, 1024, kSw128),
                         sdesc(sb + wy::tw + kk * 2048, 8192, 1024, kSw128), id_n, kk > 0);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::k0 + (kk & 3) * 2048, 16384, 1024, kSw128),
+        mma_f16_ss_warp(tmem + 128, sdesc(sb + wy::kbar + (kk & 3) * 2048, 8192, 1024, kSw128),
                         kk < 4 ? sdesc(sb + wy::zz + (kk & 3) * 2048, 8192, 1024, kSw128)
                                : sdesc(sb + wy::v0 + (kk & 3) * 2048, 16384, 1024, kSw128),
                         id_n, kk > 0);
       mma_commit_warp(&bars[wy::B_NCFULL]);
+      if (has_next) {
+        load_q(nt0, nhh, nbb);  // epilogue C was the last reader of q
+        // v's buffer holds U_lo until the N / c products complete
+        ok = mbar_wait_warp(&bars[wy::B_NCFULL], ph, abort_flag);
+        if (!ok) break;
+        load_v(nt0, nhh, nbb);
+      }
     }
     if (!ok && lane == 0) *abort_flag = 1;
     __syncwarp();
+    if (!ok) {
+      // a failed wait: let the loads in flight land before the CTA releases its smem
+      if (lane == 0) {
+        volatile int never = 0;
+        if (nk) mbar_wait(&bars[wy::B_FULLK], (nk - 1) & 1, &never);
+        if (nq) mbar_wait(&bars[wy::B_FULLQ], (nq - 1) & 1, &never);
+        if (nv) mbar_wait(&bars[wy::B_FULLV], (nv - 1) & 1, &never);
+      }
+      __syncwarp();
+    }
   } else {
     // ------------------------------------------------ prep (warps 0-7)
     constexpr int NP = wy::kPrep;
     const int ptid = tid;                     // 0..255
     const int lq = warp & 3, hc = warp >> 2;  // TMEM lane quarter, column half
     const int r = (lq << 5) | lane;           // TMEM lane = row of an M=128 accumulator
-    const float b2first = vec[V_B2 * kC], b2last = vec[V_B2 * kC + kC - 1];
-    const float ref = 0.5f * (b2first + b2last);
-    const bool prod_form = (b2first - b2last) < 200.f;
-    if (ptid < 64) amat[ptid * kAStride + 64] = fast_exp2(ref - vec[V_B2 * kC + ptid]);
-    named_bar(2, NP);
-    if (P.flags & GDN_FLAG_QK_L2NORM) {
-      // raw q and k: every row divided by sqrt(sum of squares + 1e-6) in fp32, in
-      // place, before any product reads them (gdn_ref.py:24-25).  Thread pair
-      // (2i, 2i+1) takes the two 64-column blocks of row i (k rows, then q rows).
-      if (mbar_wait_warp(&bars[wy::B_FULL], 0, abort_flag)) {
-        const int rr = ptid >> 1, half = ptid & 1, t = rr & 63;
-        uint8_t* blk = sm + (rr < 64 ? wy::k0 : wy::q0) + half * 16384;
-        uint4 xv[8];
-        float ss = 0.f;
+    for (int it = 0; it < my_n; ++it) {
+      const uint32_t ph = uint32_t(it) & 1u;
+      int il, bh;
+      wy_item<kBlocked>(P, int(blockIdx.x) + it * G, il, bh);
+      uint8_t* const pkg = P.packets + (size_t(bh) * P.NS + il) * kPacketBytes;
+      const float* vec = reinterpret_cast<const float*>(sm + wy::vec + ph * wy::kVecBytes);
+      bool ok = mbar_wait_warp(&bars[wy::B_VEC], ph, abort_flag);
+      if (bar_any(1, NP, !ok || *abort_flag)) break;
+      const float b2first = vec[V_B2 * kC], b2last = vec[V_B2 * kC + kC - 1];
+      const float ref = 0.5f * (b2first + b2last);
+      const bool prod_form = (b2first - b2last) < 200.f;
+      if (ptid < 64) amat[ptid * kAStride + 64] = fast_exp2(ref - vec[V_B2 * kC + ptid]);
+      named_bar(2, NP);
+      if (P.flags & GDN_FLAG_QK_L2NORM) {
+        // raw q and k: every row divided by sqrt(sum of squares + 1e-6) in fp32, in
+        // place, before any product reads them (gdn_ref.py:24-25).  Thread pair
+        // (2i, 2i+1) takes the two 64-column blocks of row i (k rows, then q rows).
+        if (mbar_wait_warp(&bars[wy::B_FULLK], ph, abort_flag) && mbar_wait_warp(&bars[wy::B_FULLQ], ph, abort_flag)) {
+          const int rr = ptid >> 1, half = ptid & 1, t = rr & 63;
+          uint8_t* blk = sm + (rr < 64 ? wy::k0 : wy::q0) + half * 16384;
+          uint4 xv[8];
+          float ss = 0.f;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          xv[c] = *reinterpret_cast<const uint4*>(blk + sw128_off(t, c));
-          const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+          for (int c = 0; c < 8; ++c) {
+            xv[c] = *reinterpret_cast<const uint4*>(blk + sw128_off(t, c));
+            const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = Cvt<InT>::unpack(w4[e]);
-            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
-          }
-        }
-        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-        const float inv = 1.f / sqrtf(ss + 1e-6f);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
-          uint32_t y4[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = Cvt<InT>::unpack(w4[e]);
-            y4[e] = Cvt<InT>::pack(f.x * inv, f.y * inv);
-          }
-          *reinterpret_cast<uint4*>(blk + sw128_off(t, c)) = make_uint4(y4[0], y4[1], y4[2], y4[3]);
-        }
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[wy::B_NORM]);
-    }
-    ok = mbar_wait_warp(&bars[wy::B_SFULL], 0, abort_flag);
-    if (ptid == 0) WY_TR(2);
-    if (bar_any(1, NP, !ok || *abort_flag)) ok = false;
-    if (ok) {
-      tc_fence_after();
-      // rows 0-63: A[t][m] = beta_t exp(b_t - b_m) (k_t.k_m), m < t   (TMEM lanes 0-63 = K K^T)
-      // rows 64-127: P[t][m] = exp(b_t - b_m) (q_t.k_m), m <= t      (lanes 64-127 = Q K^T)
-      const int t = r & 63;
-      const float b2t = vec[V_B2 * kC + t];
-      const float et = fast_exp2(b2t - ref);
-      const float bt = (r < 64) ? vec[V_BETA * kC + t] : 1.f;
-      float* arow = amat + t * kAStride;
-      uint8_t* pimg = sm + wy::p16;
-#pragma unroll 1
-      for (int cg = 2 * hc; cg < 2 * hc + 2; ++cg) {
-        float sv[16];
-        tmem_ld16w(tmem_addr(tmem, lq * 32, cg * 16), sv);
-        float x[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int m = cg * 16 + e;
-          const float dec = prod_form ? et * amat[m * kAStride + 64] : fast_exp2(b2t - vec[V_B2 * kC + m]);
-          const bool keep = (r < 64) ? (m < t) : (m <= t);
-          x[e] = keep ? bt * dec * sv[e] : 0.f;
-        }
-        if (r < 64) {
-#pragma unroll
-          for (int e = 0; e < 16; e += 4)
-            *reinterpret_cast<float4*>(arow + cg * 16 + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
-        } else {
-          *reinterpret_cast<uint4*>(pimg + sw128_off(t, 2 * cg)) = pack8_f16(x);
-          *reinterpret_cast<uint4*>(pimg + sw128_off(t, 2 * cg + 1)) = pack8_f16(x + 8);
-        }
-      }
-      tc_fence_before();
-      named_bar(1, NP);
-      if (ptid == 0) WY_TR(3);
-      if (P.flags & GDN_FLAG_SOLVER_NS)
-        ok = ns_solve64<NP>(amat, sm + wy::tw, sm + wy::tw + 8192, sm + wy::zz, tmem, &bars[wy::B_NSR],
-                            &bars[wy::B_NSD], (P.flags >> GDN_FLAG_NS_ITERS_SHIFT) & 15, abort_flag);
-      else
-        invert_unit_lower64<NP>(amat, ptid);  // T = (I + A)^-1 in place
-      if (ptid == 0) WY_TR(4);
-      // Tw = T diag(beta e^b), Tb = T diag(beta), each split hi + lo in the input dtype:
-      // [Tw_hi; Tb_hi] and [Tw_lo; Tb_lo]
-      {
-        const int rr = ptid >> 2, cq = ptid & 3;
-        const float* trow = amat + rr * kAStride;
-        uint8_t* twh = sm + wy::tw;
-        uint8_t* tbh = sm + wy::tw + 8192;
-        uint8_t* twl = sm + wy::zz;
-        uint8_t* tbl = sm + wy::zz + 8192;
-#pragma unroll
-        for (int c = 2 * cq; c < 2 * cq + 2; ++c) {
-          uint32_t wh[4], wl[4], hi[4], lo[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int m = 8 * c + 2 * e;
-            const float tb0 = trow[m] * vec[V_BETA * kC + m], tb1 = trow[m + 1] * vec[V_BETA * kC + m + 1];
-            const float tw0 = tb0 * vec[V_EB * kC + m], tw1 = tb1 * vec[V_EB * kC + m + 1];
-            wh[e] = Cvt<InT>::pack(tw0, tw1);
-            const float2 wf = Cvt<InT>::unpack(wh[e]);
-            wl[e] = Cvt<InT>::pack(tw0 - wf.x, tw1 - wf.y);
-            hi[e] = Cvt<InT>::pack(tb0, tb1);
-            const float2 hf = Cvt<InT>::unpack(hi[e]);
-            lo[e] = Cvt<InT>::pack(tb0 - hf.x, tb1 - hf.y);
-          }
-          const uint32_t off = sw128_off(rr, c);
-          *reinterpret_cast<uint4*>(twh + off) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-          *reinterpret_cast<uint4*>(twl + off) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
-          *reinterpret_cast<uint4*>(tbh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-          *reinterpret_cast<uint4*>(tbl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        }
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[wy::B_TREADY]);
-      if (ptid == 0) WY_TR(5);
-    }
-    // ---- epilogue A: rows 0-63 W -> fp16 [t][k] (over [Tw; Tb_hi]); rows 64-127 U -> fp16
-    //      hi (over [Tw_lo; Tb_lo]) and lo (over v); and k -> Kbar = e^{b_C - b_t} k fp16 in place
-    ok = ok && mbar_wait_warp(&bars[wy::B_WUFULL], 0, abort_flag);
-    if (ptid == 0) WY_TR(6);
-    if (ok) {
-      tc_fence_after();
-      const int t = r & 63;
-      const bool isw = r < 64;
-#pragma unroll 1
-      for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
-        float x[32];
-        tmem_ld32w(tmem_addr(tmem, lq * 32, (isw ? 0 : 128) + c0), x);
-        const uint32_t chunk0 = (c0 & 63) >> 3;
-        if (isw) {
-          uint8_t* dst = sm + wy::tw + (c0 >> 6) * 8192;
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(dst + sw128_off(t, chunk0 + c)) = pack8_f16(x + 8 * c);
-        } else {
-          uint8_t* dhi = sm + wy::zz + (c0 >> 6) * 8192;
-          uint8_t* dlo = sm + wy::v0 + (c0 >> 6) * 16384;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float hi[8], lo[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              hi[e] = __half2float(__float2half_rn(x[8 * c + e]));
-              lo[e] = x[8 * c + e] - hi[e];
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = Cvt<InT>::unpack(w4[e]);
+              ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
             }
-            const uint32_t off = sw128_off(t, chunk0 + c);
-            *reinterpret_cast<uint4*>(dhi + off) = pack8_f16(hi);
-            *reinterpret_cast<uint4*>(dlo + off) = pack8_f16(lo);
+          }
+          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+          const float inv = 1.f / sqrtf(ss + 1e-6f);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+            uint32_t y4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = Cvt<InT>::unpack(w4[e]);
+              y4[e] = Cvt<InT>::pack(f.x * inv, f.y * inv);
+            }
+            *reinterpret_cast<uint4*>(blk + sw128_off(t, c)) = make_uint4(y4[0], y4[1], y4[2], y4[3]);
           }
         }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[wy::B_NORM]);
       }
+      ok = mbar_wait_warp(&bars[wy::B_SFULL], ph, abort_flag);
+      if (bar_any(1, NP, !ok || *abort_flag)) break;
       {
-        const float dd = vec[V_DD * kC + t];
-        uint8_t* kb = sm + (isw ? wy::k0 : wy::k1);
-#pragma unroll
-        for (int c = 4 * hc; c < 4 * hc + 4; ++c) {
-          uint4* pp = reinterpret_cast<uint4*>(kb + sw128_off(t, c));
-          const uint4 x = *pp;
-          const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-          uint32_t ys[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = Cvt<InT>::unpack(xs[e]);
-            ys[e] = Cvt<__half>::pack(f.x * dd, f.y * dd);
-          }
-          *pp = make_uint4(ys[0], ys[1], ys[2], ys[3]);
-        }
-      }
-      fence_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[wy::B_EPA]);
-      if (ptid == 0) WY_TR(7);
-    }
-    // ---- epilogue C: Q' = e^{b_t} q_t - (P W)_t (in place over q) and o_intra = P U (M=64:
-    //      row 16 lq + l in lane 32 lq + l, l < 16)
-    ok = ok && mbar_wait_warp(&bars[wy::B_PFULL], 0, abort_flag);
-    if (ptid == 0) WY_TR(10);
-    if (bar_any(1, NP, !ok || *abort_flag)) ok = false;  // uniform: named barriers follow
-    if (ok) {
-      tc_fence_after();
-      const int t = 16 * lq + (lane & 15);
-      const float eb = vec[V_EB * kC + t];
-      const uint64_t keep = l2_policy_evict_last();  // packets: keep in L2 for the scan
+        tc_fence_after();
+        // rows 0-63: A[t][m] = beta_t exp(b_t - b_m) (k_t.k_m), m < t   (TMEM lanes 0-63 = K K^T)
+        // rows 64-127: P[t][m] = exp(b_t - b_m) (q_t.k_m), m <= t      (lanes 64-127 = Q K^T)
+        const int t = r & 63;
+        const float b2t = vec[V_B2 * kC + t];
+        const float et = fast_exp2(b2t - ref);
+        const float bt = (r < 64) ? vec[V_BETA * kC + t] : 1.f;
+        float* arow = amat + t * kAStride;
+        uint8_t* pimg = sm + wy::p16;
 #pragma unroll 1
-      for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
-        float pw[32];
-        tmem_ld32w(tmem_addr(tmem, lq * 32, c0), pw);
-        if (lane < 16) {
-          const uint8_t* qrow = sm + wy::q0 + (c0 >> 6) * 16384;
+        for (int cg = 2 * hc; cg < 2 * hc + 2; ++cg) {
+          float sv[16];
+          tmem_ld16w(tmem_addr(tmem, lq * 32, cg * 16), sv);
+          float x[16];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 x = *reinterpret_cast<const uint4*>(qrow + sw128_off(t, ((c0 & 63) >> 3) + c));
+          for (int e = 0; e < 16; ++e) {
+            const int m = cg * 16 + e;
+            const float dec = prod_form ? et * amat[m * kAStride + 64] : fast_exp2(b2t - vec[V_B2 * kC + m]);
+            const bool keep = (r < 64) ? (m < t) : (m <= t);
+            x[e] = keep ? bt * dec * sv[e] : 0.f;
+          }
+          if (r < 64) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 4)
+              *reinterpret_cast<float4*>(arow + cg * 16 + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+          } else {
+            *reinterpret_cast<uint4*>(pimg + sw128_off(t, 2 * cg)) = pack8_f16(x);
+            *reinterpret_cast<uint4*>(pimg + sw128_off(t, 2 * cg + 1)) = pack8_f16(x + 8);
+          }
+        }
+        tc_fence_before();
+        named_bar(1, NP);
+        if (P.flags & GDN_FLAG_SOLVER_NS)
+          ok = ns_solve64<NP>(amat, sm + wy::tw, sm + wy::tw + 8192, sm + wy::zz, tmem, &bars[wy::B_NSR],
+                              &bars[wy::B_NSD], (P.flags >> GDN_FLAG_NS_ITERS_SHIFT) & 15, abort_flag);
+        else
+          invert_unit_lower64<NP>(amat, ptid);  // T = (I + A)^-1 in place
+        if (!ok) break;  // uniform: ns_solve64 decides through bar_any
+        // Tw = T diag(beta e^b), Tb = T diag(beta), each split hi + lo in the input dtype:
+        // [Tw_hi; Tb_hi] and [Tw_lo; Tb_lo]
+        {
+          const int rr = ptid >> 2, cq = ptid & 3;
+          const float* trow = amat + rr * kAStride;
+          uint8_t* twh = sm + wy::tw;
+          uint8_t* tbh = sm + wy::tw + 8192;
+          uint8_t* twl = sm + wy::zz;
+          uint8_t* tbl = sm + wy::zz + 8192;
+#pragma unroll
+          for (int c = 2 * cq; c < 2 * cq + 2; ++c) {
+            uint32_t wh[4], wl[4], hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int m = 8 * c + 2 * e;
+              const float tb0 = trow[m] * vec[V_BETA * kC + m], tb1 = trow[m + 1] * vec[V_BETA * kC + m + 1];
+              const float tw0 = tb0 * vec[V_EB * kC + m], tw1 = tb1 * vec[V_EB * kC + m + 1];
+              wh[e] = Cvt<InT>::pack(tw0, tw1);
+              const float2 wf = Cvt<InT>::unpack(wh[e]);
+              wl[e] = Cvt<InT>::pack(tw0 - wf.x, tw1 - wf.y);
+              hi[e] = Cvt<InT>::pack(tb0, tb1);
+              const float2 hf = Cvt<InT>::unpack(hi[e]);
+              lo[e] = Cvt<InT>::pack(tb0 - hf.x, tb1 - hf.y);
+            }
+            const uint32_t off = sw128_off(rr, c);
+            *reinterpret_cast<uint4*>(twh + off) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+            *reinterpret_cast<uint4*>(twl + off) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+            *reinterpret_cast<uint4*>(tbh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(tbl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          }
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[wy::B_TREADY]);
+        // A / T is dead from here; epilogue A writes Kbar over it once the W | U
+        // product, issued after every warp's B_TREADY arrival, has completed
+      }
+      // ---- epilogue A: rows 0-63 W -> fp16 [t][k] (over [Tw; Tb_hi]); rows 64-127 U -> fp16
+      //      hi (over [Tw_lo; Tb_lo]) and lo (over v); and Kbar = e^{b_C - b_t} k fp16 (over A / T)
+      ok = mbar_wait_warp(&bars[wy::B_WUFULL], ph, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        const int t = r & 63;
+        const bool isw = r < 64;
+#pragma unroll 1
+        for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
+          float x[32];
+          tmem_ld32w(tmem_addr(tmem, lq * 32, (isw ? 0 : 128) + c0), x);
+          const uint32_t chunk0 = (c0 & 63) >> 3;
+          if (isw) {
+            uint8_t* dst = sm + wy::tw + (c0 >> 6) * 8192;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              *reinterpret_cast<uint4*>(dst + sw128_off(t, chunk0 + c)) = pack8_f16(x + 8 * c);
+          } else {
+            uint8_t* dhi = sm + wy::zz + (c0 >> 6) * 8192;
+            uint8_t* dlo = sm + wy::v0 + (c0 >> 6) * 16384;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              float hi[8], lo[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                hi[e] = __half2float(__float2half_rn(x[8 * c + e]));
+                lo[e] = x[8 * c + e] - hi[e];
+              }
+              const uint32_t off = sw128_off(t, chunk0 + c);
+              *reinterpret_cast<uint4*>(dhi + off) = pack8_f16(hi);
+              *reinterpret_cast<uint4*>(dlo + off) = pack8_f16(lo);
+            }
+          }
+        }
+        {
+          const float dd = vec[V_DD * kC + t];
+          const uint8_t* ks = sm + (isw ? wy::k0 : wy::k1);
+          uint8_t* kd = sm + wy::kbar + (isw ? 0 : 8192);
+#pragma unroll
+          for (int c = 4 * hc; c < 4 * hc + 4; ++c) {
+            const uint4 x = *reinterpret_cast<const uint4*>(ks + sw128_off(t, c));
             const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-            float y[8];
+            uint32_t ys[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 f = Cvt<InT>::unpack(xs[e]);
-              y[2 * e] = fmaf(eb, f.x, -pw[8 * c + 2 * e]) * P.scale;
-              y[2 * e + 1] = fmaf(eb, f.y, -pw[8 * c + 2 * e + 1]) * P.scale;
+              ys[e] = Cvt<__half>::pack(f.x * dd, f.y * dd);
             }
-            const int j = (c0 >> 3) + c;  // 16-byte chunk of the 128 Q' columns
-            st_global_hint(pkg + pkt::kQ + (j * 64 + t) * 16, pack8_f16(y), keep);
+            *reinterpret_cast<uint4*>(kd + sw128_off(t, c)) = make_uint4(ys[0], ys[1], ys[2], ys[3]);
           }
         }
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[wy::B_EPA]);
       }
+      // ---- epilogue C: Q' = e^{b_t} q_t - (P W)_t and o_intra = P U (M=64: row 16 lq + l in
+      //      lane 32 lq + l, l < 16), straight to the packet; e^{b_C}
+      ok = ok && mbar_wait_warp(&bars[wy::B_PFULL], ph, abort_flag);
+      if (bar_any(1, NP, !ok || *abort_flag)) break;  // uniform: named barriers follow
+      {
+        tc_fence_after();
+        const int t = 16 * lq + (lane & 15);
+        const float eb = vec[V_EB * kC + t];
+        const uint64_t keep = l2_policy_evict_last();  // packets: keep in L2 for the scan
 #pragma unroll 1
-      for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
-        float ou[32];
-        tmem_ld32w(tmem_addr(tmem, lq * 32, 128 + c0), ou);
-        if (lane < 16) {
-          uint8_t* dst = pkg + pkt::kOs + (c0 >> 5) * 4096;  // V slice c0 / 32
+        for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
+          float pw[32];
+          tmem_ld32w(tmem_addr(tmem, lq * 32, c0), pw);
+          if (lane < 16) {
+            const uint8_t* qrow = sm + wy::q0 + (c0 >> 6) * 16384;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint4 x = *reinterpret_cast<const uint4*>(qrow + sw128_off(t, ((c0 & 63) >> 3) + c));
+              const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+              float y[8];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = Cvt<InT>::unpack(xs[e]);
+                y[2 * e] = fmaf(eb, f.x, -pw[8 * c + 2 * e]) * P.scale;
+                y[2 * e + 1] = fmaf(eb, f.y, -pw[8 * c + 2 * e + 1]) * P.scale;
+              }
+              const int j = (c0 >> 3) + c;  // 16-byte chunk of the 128 Q' columns
+              st_global_hint(pkg + pkt::kQ + (j * 64 + t) * 16, pack8_f16(y), keep);
+            }
+          }
+        }
+#pragma unroll 1
+        for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
+          float ou[32];
+          tmem_ld32w(tmem_addr(tmem, lq * 32, 128 + c0), ou);
+          if (lane < 16) {
+            uint8_t* dst = pkg + pkt::kOs + (c0 >> 5) * 4096;  // V slice c0 / 32
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              float sc8[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) sc8[e] = ou[8 * c + e] * P.scale;
+              st_global_hint(dst + (c * 64 + t) * 16, pack8_f16(sc8), keep);
+            }
+          }
+        }
+        if (ptid == 0) *reinterpret_cast<float*>(pkg + pkt::kHdr) = vec[V_EB * kC + kC - 1];
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[wy::B_EPC]);
+      }
+      // ---- epilogue B: N = -(Kbar^T W) and c = Kbar^T U (row k1 = TMEM lane)
+      ok = mbar_wait_warp(&bars[wy::B_NCFULL], ph, abort_flag);
+      if (bar_any(1, NP, !ok || *abort_flag)) break;
+      {
+        tc_fence_after();
+        const uint64_t keep = l2_policy_evict_last();
+#pragma unroll 1
+        for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
+          float n[32];
+          tmem_ld32w(tmem_addr(tmem, lq * 32, c0), n);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) n[e] = -n[e];
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            float sc8[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) sc8[e] = ou[8 * c + e] * P.scale;
-            st_global_hint(dst + (c * 64 + t) * 16, pack8_f16(sc8), keep);
+            const int j = (c0 >> 3) + c;  // 16-byte chunk of the 128 N columns
+            st_global_hint(pkg + pkt::kN + (j * 128 + r) * 16, pack8_f16(n + 8 * c), keep);
           }
         }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[wy::B_EPC]);
-      if (ptid == 0) WY_TR(11);
-    }
-    // ---- epilogue B: N = -(Kbar^T W) and c = Kbar^T U (row k1 = TMEM lane)
-    ok = ok && mbar_wait_warp(&bars[wy::B_NCFULL], 0, abort_flag);
-    if (ptid == 0) WY_TR(8);
-    if (bar_any(1, NP, !ok || *abort_flag)) ok = false;
-    if (ok) {
-      tc_fence_after();
-      const uint64_t keep = l2_policy_evict_last();
 #pragma unroll 1
-      for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
-        float n[32];
-        tmem_ld32w(tmem_addr(tmem, lq * 32, c0), n);
+        for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
+          float cv[32];
+          tmem_ld32w(tmem_addr(tmem, lq * 32, 128 + c0), cv);
+          uint8_t* dst = pkg + pkt::kCs + (c0 >> 5) * 8192;  // V slice c0 / 32
 #pragma unroll
-        for (int e = 0; e < 32; ++e) n[e] = -n[e];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int j = (c0 >> 3) + c;  // 16-byte chunk of the 128 N columns
-          st_global_hint(pkg + pkt::kN + (j * 128 + r) * 16, pack8_f16(n + 8 * c), keep);
+          for (int c = 0; c < 4; ++c) st_global_hint(dst + (c * 128 + r) * 16, pack8_f16(cv + 8 * c), keep);
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[wy::B_EPB]);
       }
-#pragma unroll 1
-      for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
-        float cv[32];
-        tmem_ld32w(tmem_addr(tmem, lq * 32, 128 + c0), cv);
-        uint8_t* dst = pkg + pkt::kCs + (c0 >> 5) * 8192;  // V slice c0 / 32
-#pragma unroll
-        for (int c = 0; c < 4; ++c) st_global_hint(dst + (c * 128 + r) * 16, pack8_f16(cv + 8 * c), keep);
-      }
-      if (ptid == 0) *reinterpret_cast<float*>(pkg + pkt::kHdr) = vec[V_EB * kC + kC - 1];
-      tc_fence_before();
-      if (ptid == 0) WY_TR(9);
     }
-    if (!ok) *abort_flag = 1;
   }
   __syncthreads();
   if (warp == wy::kMmaWarp) {
-    if (lane == 0 && *abort_flag) {
-      // a failed wait: let the TMA loads land before the CTA releases its smem
-      volatile int never = 0;
-      mbar_wait(&bars[wy::B_FULL], 0, &never);
-      mbar_wait(&bars[wy::B_FULLV], 0, &never);
-      if (P.status != nullptr) atomicOr(P.status, 1 << GDN_ERR_TIMEOUT);
-    }
+    if (lane == 0 && *abort_flag && P.status != nullptr) atomicOr(P.status, 1 << GDN_ERR_TIMEOUT);
     __syncwarp();
     // every issued MMA completes before TMEM is released (same elected lane as the MMAs)
     mma_commit_warp(&bars[wy::B_DONE]);
@@ -701,10 +773,6 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 256);
-    if (lane == 0) WY_TR(12);
-#ifdef GDN_TRACE
-    if (lane == 0 && WY_TRACED()) P.trace[(blockIdx.x - GDN_TRACE_BASE) * 24 + 21] = (long long)globaltimer();
-#endif
   }
 }
 
@@ -1007,7 +1075,10 @@ int launch_scan(const ScanParams& p, int grid, cudaStream_t s) {
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
 }
 
-int run_wy(int in_bf16, const WyParams& p, int grid, cudaStream_t s) {
+int run_wy(int in_bf16, const WyParams& p, int num_sms, cudaStream_t s) {
+  const long long items = (long long)p.B * p.H * p.NS;
+  const int grid = int(items < 2LL * num_sms ? items : 2LL * num_sms);
+  if (grid < 1) return GDN_OK;
   if (p.blk_len < p.NS)
     return in_bf16 ? launch_wy<__nv_bfloat16, true>(p, grid, s) : launch_wy<__half, true>(p, grid, s);
   return in_bf16 ? launch_wy<__nv_bfloat16, false>(p, grid, s) : launch_wy<__half, false>(p, grid, s);

@@ -9,7 +9,8 @@
 namespace gdn {
 
 // Chunk-parallel prep: reads q, k, v (TMA, 64-column boxes, 128B swizzle),
-// beta and g; writes one packet per (b, h, chunk).
+// beta and g; writes one packet per (b, h, chunk).  Persistent: launched with
+// at most two CTAs per SM, each taking every G-th item (chunk) of the segment.
 struct WyParams {
   CUtensorMap tm_q, tm_k, tm_v;
   const float* beta;
@@ -22,8 +23,7 @@ struct WyParams {
   int B, T, H, c0, NS;  // segment = chunks [c0, c0 + NS)
   float scale;          // multiplies Q' and o_intra (q scaled)
   int flags;            // GDN_FLAG_*
-  int pf_stride;        // CTAs resident at once (2 per SM): blockIdx + pf_stride is prefetched to L2
-  int blk_len;          // chunks per block of the CTA order (NS: one block): see wy_cta_chunk
+  int blk_len;          // chunks per block of the item order (NS: one block): see wy_item_blocked
 };
 
 // Serial scan over the packets of one segment.
@@ -41,7 +41,8 @@ struct ScanParams {
 // Bytes of one packet: N and Q' images, e^{b_C}, c and o_intra slices (fp16).
 constexpr uint64_t kPacketBytesPerChunk = 98560;
 
-int run_wy(int in_bf16, const WyParams& p, int grid, cudaStream_t s);
+// Launch the prep over the segment's B * H * NS items with min(items, 2 * SMs) CTAs.
+int run_wy(int in_bf16, const WyParams& p, int num_sms, cudaStream_t s);
 // The argument checks of gdn_fwd_sm100 (a gdn_status code; GDN_OK if the
 // request is valid and supported).  Defined in gdn_fwd.cu.
 int validate_fwd_args(const ::gdn_fwd_args* a);
