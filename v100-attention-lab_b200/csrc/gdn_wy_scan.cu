@@ -75,7 +75,7 @@ constexpr uint32_t kbar = amat;
 constexpr uint32_t vec = amat + 17408;  // 2 buffers (item parity) x kVecN x 64 fp32
 constexpr uint32_t kVecBytes = kVecN * kC * 4;
 constexpr uint32_t bars = vec + 2 * kVecBytes;
-constexpr uint32_t misc = bars + 16 * 8;
+constexpr uint32_t misc = bars + 24 * 8;
 constexpr uint32_t total = misc + 32;
 constexpr uint32_t alloc = total + 1024;
 static_assert(kC * kAStride * 4 <= 17408 && 2 * 8192 <= 17408, "A/T region");
@@ -96,16 +96,19 @@ static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
 // The next item's inputs are loaded while this one finishes, each as soon as
 // its buffer is free: k after epilogue A (Kbar is out), q after epilogue C,
 // v (later U_lo) after the N / c products; its S product waits for epilogue B
-// to release TMEM.  Its g and beta are read into registers when this item
-// starts and its vectors are written (into the other of two buffers) while
-// the prep warps run this item's epilogues, so the next item's S product and
-// A / P phase wait for nothing but epilogue B (measured: vectors computed
+// to release TMEM.  Its g and beta are read and its vectors written (into the
+// other of two buffers) right after this item's S product is issued, while the
+// prep warps run the inverse, so neither the next S product nor the MMA
+// warp's response to the epilogues waits on them (measured: vectors computed
 // after the N / c issue kept the prep warps idle ~7.8k of ~30k cycles per item).
+// B_STARTED keeps the MMA warp from completing the next item's B_VEC phase
+// before every prep warp has waited on this item's.
 enum {
   B_FULLK = 0,  // k landed
   B_FULLQ,      // q landed
   B_FULLV,      // v landed (first read by the W | U product)
   B_VEC,        // the item's cumsum / beta vectors written (MMA warp)
+  B_STARTED,    // every prep warp has passed the item's B_VEC wait
   B_SFULL,
   B_TREADY,
   B_WUFULL,
@@ -120,7 +123,7 @@ enum {
   B_DONE,
   B_COUNT
 };
-static_assert(B_COUNT <= 16, "barrier region");
+static_assert(B_COUNT <= 24, "barrier region");
 }  // namespace wy
 
 __device__ __forceinline__ uint4 pack8_f16(const float* x) {
@@ -302,7 +305,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     if (lane == 0) {
       for (int i = 0; i < wy::B_COUNT; ++i)
         mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC || i == wy::B_EPB ||
-                             i == wy::B_NORM || i == wy::B_NSR)
+                             i == wy::B_NORM || i == wy::B_NSR || i == wy::B_STARTED)
                                 ? wy::kPrep / 32
                                 : 1);
       *abort_flag = 0;
@@ -361,7 +364,6 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       const uint32_t ph = uint32_t(it) & 1u;
       const bool has_next = it + 1 < my_n;
       int nt0 = 0, nhh = 0, nbb = 0;
-      WyStepVals nsv = {0.f, 0.f, 0.f, 0.f};
       if (has_next) {
         int nil, nbh;
         wy_item<kBlocked>(P, int(blockIdx.x) + (it + 1) * G, nil, nbh);
@@ -376,7 +378,6 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
           tma_prefetch_4d(&P.tm_v, 0, nt0, nhh, nbb);
           tma_prefetch_4d(&P.tm_v, 64, nt0, nhh, nbb);
         }
-        nsv = wy_step_vals(P, nbb, nhh, nt0, lane);  // used after the W | U issue
       }
       ok = mbar_wait_warp(&bars[wy::B_FULLK], ph, abort_flag) && mbar_wait_warp(&bars[wy::B_FULLQ], ph, abort_flag);
       if (P.flags & GDN_FLAG_QK_L2NORM) ok = ok && mbar_wait_warp(&bars[wy::B_NORM], ph, abort_flag);
@@ -391,6 +392,18 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         mma_f16_ss_warp(tmem, sdesc(a, 16, 1024, kSw128), sdesc(a, 16, 1024, kSw128), id_s, kk > 0);
       }
       mma_commit_warp(&bars[wy::B_SFULL]);
+      if (has_next) {
+        // the next item's vectors into the other buffer, while the prep warps
+        // run A / P and the inverse: that buffer's previous item read it for
+        // the last time in its epilogue C, and B_STARTED says every prep warp
+        // has waited on this item's B_VEC phase
+        const WyStepVals nsv = wy_step_vals(P, nbb, nhh, nt0, lane);
+        ok = mbar_wait_warp(&bars[wy::B_STARTED], ph, abort_flag);
+        if (!ok) break;
+        wy_vectors(nsv, vec_buf + (ph ^ 1u) * (wy::kVecBytes / 4), lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[wy::B_VEC]);
+      }
       // Newton-Schulz solve (gdn_triton_v2.py:58-68): per iteration M X, then X (2I - M X),
       // fp16 operands written by the prep warps: M at tw, X at tw + 8 KB, 2I - M X at zz
       const int ns_iters = (P.flags >> GDN_FLAG_NS_ITERS_SHIFT) & 15;
@@ -426,14 +439,6 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         mma_f16_ss_warp(tmem, sdesc(sb + (kk < 4 ? wy::tw : wy::zz) + (kk & 3) * 32, 16, 1024, kSw128),
                         sdesc(sb + wy::k0 + (kk & 3) * 2048, 16384, 1024, kSw128), id_wu, kk > 0);
       mma_commit_warp(&bars[wy::B_WUFULL]);
-      if (has_next) {
-        // the next item's vectors into the other buffer: every prep warp has
-        // passed this item's B_VEC wait (they arrived on B_TREADY), and that
-        // buffer's previous item read it for the last time in its epilogue C
-        wy_vectors(nsv, vec_buf + (ph ^ 1u) * (wy::kVecBytes / 4), lane);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[wy::B_VEC]);
-      }
       ok = mbar_wait_warp(&bars[wy::B_EPA], ph, abort_flag);
       if (!ok) break;
       if (has_next) load_k(nt0, nhh, nbb);  // epilogue A has read k and written Kbar elsewhere
@@ -501,6 +506,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       const float* vec = reinterpret_cast<const float*>(sm + wy::vec + ph * wy::kVecBytes);
       bool ok = mbar_wait_warp(&bars[wy::B_VEC], ph, abort_flag);
       if (bar_any(1, NP, !ok || *abort_flag)) break;
+      if (lane == 0) mbar_arrive(&bars[wy::B_STARTED]);
       const float b2first = vec[V_B2 * kC], b2last = vec[V_B2 * kC + kC - 1];
       const float ref = 0.5f * (b2first + b2last);
       const bool prod_form = (b2first - b2last) < 200.f;
