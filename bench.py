@@ -319,7 +319,7 @@ def launches_per_forward(B, T, H):
     segment of chunks that fits the (capped) workspace."""
     from gdn_b200 import _lib, ops
     nt = -(-T // CHUNK)
-    state = B * H * K_DIM * V_DIM * 4
+    state = B * H * K_DIM * V_DIM * 4 + _lib.WORKSPACE_HEADER_BYTES
     per_chunk = B * H * _lib.PACKET_BYTES_PER_CHUNK
     need = nt * per_chunk + state
     ws = max(min(need, ops.WORKSPACE_CAP_BYTES), per_chunk + state)

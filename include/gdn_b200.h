@@ -133,9 +133,11 @@ int gdn_fwd_sm100(const gdn_fwd_args* args, void* stream);
 
 /*
  * Workspace bytes that let gdn_fwd_sm100 run the whole sequence as one
- * segment: B*H*ceil(T/C)*98560 + B*H*V*K*4 (state carried between segments).
- * Any smaller workspace of at least B*H*(98560 + V*K*4) bytes works with more
- * segments.  Returns 0 for invalid arguments.
+ * segment: 256 + B*H*ceil(T/C)*98560 + B*H*V*K*4 (a 256-byte header for the
+ * prep kernel's work counter, which each call zeroes itself, and the state
+ * carried between segments).  Any smaller workspace of at least
+ * 256 + B*H*(98560 + V*K*4) bytes works with more segments.  Its contents need
+ * no initialisation.  Returns 0 for invalid arguments.
  */
 uint64_t gdn_fwd_workspace_bytes(const gdn_fwd_args* args);
 
@@ -147,8 +149,9 @@ uint64_t gdn_fwd_workspace_bytes(const gdn_fwd_args* args);
  * synchronisation cudaMalloc may cause.  It runs the two-kernel path with its
  * scratch in a fixed GDN_NOALLOC_SCRATCH_BYTES array inside the library
  * (args->workspace is ignored) and makes no allocation itself.
- * - Limit: B*H*(98560 + V*K*4) bytes must fit in the array (one chunk of
- *   operands plus one fp32 state per (batch, head)); larger requests return
+ * - Limit: 256 + B*H*(98560 + V*K*4) bytes must fit in the array (a work
+ *   counter, one chunk of operands and one fp32 state per (batch, head));
+ *   larger requests return
  *   GDN_ERR_SCRATCH_LIMIT before any device work.  Longer sequences are run
  *   in as many segments of chunks as the array requires.
  * - Invalid or unsupported requests return the same codes as gdn_fwd_sm100,

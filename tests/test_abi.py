@@ -126,7 +126,8 @@ def test_workspace_query(lib):
     from gdn_b200 import _lib
     pk = _lib.PACKET_BYTES_PER_CHUNK
     # one packet per (b, h, chunk) plus one fp32 state per (b, h)
-    assert lib.gdn_fwd_workspace_bytes(ctypes.byref(a)) == 2 * 16 * (64 * pk + 128 * 128 * 4)
+    hdr = _lib.WORKSPACE_HEADER_BYTES
+    assert lib.gdn_fwd_workspace_bytes(ctypes.byref(a)) == hdr + 2 * 16 * (64 * pk + 128 * 128 * 4)
     a = _args(T=100)
-    assert lib.gdn_fwd_workspace_bytes(ctypes.byref(a)) == 1 * 1 * (2 * pk + 128 * 128 * 4)
+    assert lib.gdn_fwd_workspace_bytes(ctypes.byref(a)) == hdr + 1 * 1 * (2 * pk + 128 * 128 * 4)
     assert lib.gdn_fwd_workspace_bytes(None) == 0

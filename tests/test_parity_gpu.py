@@ -82,7 +82,7 @@ def test_segmented_workspace(gdn, cap_chunks, monkeypatch):
     the state carried between them."""
     from gdn_b200 import _lib, ops
     B, H = 1, 2
-    cap = B * H * (cap_chunks * _lib.PACKET_BYTES_PER_CHUNK + 128 * 128 * 4)
+    cap = _lib.WORKSPACE_HEADER_BYTES + B * H * (cap_chunks * _lib.PACKET_BYTES_PER_CHUNK + 128 * 128 * 4)
     monkeypatch.setattr(ops, "WORKSPACE_CAP_BYTES", cap)
     monkeypatch.setattr(ops, "_workspaces", {})
     qd, kd, vd, bd, gd, h0 = make(B, 450, H, seed=42, dtype=torch.float16, h0_std=0.1)

@@ -237,6 +237,106 @@ __device__ __forceinline__ void inv_level(float* am, int tid) {
   named_bar(1, NTH);
 }
 
+// One doubling level with the intermediate Y = X inv(L0) in a scratch tile
+// instead of in place over X, so each phase ends with a single barrier (the
+// in-place form needs one between computing and writing back): 2 barriers per
+// level instead of 4.  Same arithmetic, same order of operations.  `scr` holds
+// (64 / 2N) blocks of N rows at a stride of N + 4 floats (at most 4.5 KB) and
+// must not overlap `am`.
+template <int N, int NTH>
+__device__ __forceinline__ void inv_level_scr(float* am, float* scr, int tid) {
+  using It = InvItems<N, NTH>;
+  constexpr int S = kAStride;
+  constexpr int SS = N + 4;
+  // phase 1: Y = X inv(L0) -> scr; X = rows N..2N-1 x cols 0..N-1 of each 2N block
+#pragma unroll
+  for (int e = 0; e < It::PER; ++e) {
+    int blk, i, q;
+    if (It::p1(tid, e, blk, i, q)) {
+      float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+      const int o = blk * 2 * N;
+      const float* xr = am + (o + N + i) * S + o;
+#pragma unroll
+      for (int m4 = 0; m4 < It::NQ; ++m4) {
+        if (m4 >= q) {
+          const float4 x = *reinterpret_cast<const float4*>(xr + 4 * m4);
+          const float* t0 = am + (o + 4 * m4) * S + o + 4 * q;
+          fma4(a0, x.x, *reinterpret_cast<const float4*>(t0));
+          fma4(a1, x.y, *reinterpret_cast<const float4*>(t0 + S));
+          fma4(a0, x.z, *reinterpret_cast<const float4*>(t0 + 2 * S));
+          fma4(a1, x.w, *reinterpret_cast<const float4*>(t0 + 3 * S));
+        }
+      }
+      *reinterpret_cast<float4*>(scr + (blk * N + i) * SS + 4 * q) =
+          make_float4(a0.x + a1.x, a0.y + a1.y, a0.z + a1.z, a0.w + a1.w);
+    }
+  }
+  named_bar(1, NTH);
+  // phase 2: T21 = -inv(L1) Y over X (X's last reader was phase 1)
+#pragma unroll
+  for (int e = 0; e < It::PER; ++e) {
+    int blk, i, q;
+    if (It::p2(tid, e, blk, i, q)) {
+      float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+      const int o = blk * 2 * N;
+      const float* tr = am + (o + N + i) * S + o + N;
+      const float* yb = scr + (blk * N) * SS + 4 * q;
+#pragma unroll
+      for (int p4 = 0; p4 < It::NQ; ++p4) {
+        if (p4 <= (i >> 2)) {
+          const float4 t = *reinterpret_cast<const float4*>(tr + 4 * p4);
+          const float* y = yb + (4 * p4) * SS;
+          fma4(a0, t.x, *reinterpret_cast<const float4*>(y));
+          fma4(a1, t.y, *reinterpret_cast<const float4*>(y + SS));
+          fma4(a0, t.z, *reinterpret_cast<const float4*>(y + 2 * SS));
+          fma4(a1, t.w, *reinterpret_cast<const float4*>(y + 3 * SS));
+        }
+      }
+      *reinterpret_cast<float4*>(am + (o + N + i) * S + o + 4 * q) =
+          make_float4(-(a0.x + a1.x), -(a0.y + a1.y), -(a0.z + a1.z), -(a0.w + a1.w));
+    }
+  }
+  named_bar(1, NTH);
+}
+
+// The diagonal 8x8 blocks of (I + A)^-1 by column forward substitution
+// (64 threads), in place.
+__device__ __forceinline__ void invert_diag8(float* am, int ptid) {
+  if (ptid < 64) {
+    const int blk_id = ptid >> 3, c = ptid & 7;
+    float* blk = am + (8 * blk_id) * kAStride + 8 * blk_id;
+    float x[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) x[m] = (m == c) ? 1.f : 0.f;
+#pragma unroll
+    for (int t = 1; t < 8; ++t) {
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int m = 0; m < t; ++m) {
+        if (m & 1)
+          a1 = fmaf(blk[t * kAStride + m], x[m], a1);
+        else
+          a0 = fmaf(blk[t * kAStride + m], x[m], a0);
+      }
+      if (t > c) x[t] = -(a0 + a1);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int t = 0; t < 8; ++t) blk[t * kAStride + c] = x[t];
+  }
+}
+
+// T = (I + A)^-1 in place, as invert_unit_lower64, with the doubling levels'
+// intermediates in `scr` (>= 4608 bytes, disjoint from am): 7 barriers, not 13.
+template <int NTH>
+__device__ __forceinline__ void invert_unit_lower64_scr(float* am, float* scr, int ptid) {
+  invert_diag8(am, ptid);
+  named_bar(1, NTH);
+  inv_level_scr<8, NTH>(am, scr, ptid);
+  inv_level_scr<16, NTH>(am, scr, ptid);
+  inv_level_scr<32, NTH>(am, scr, ptid);
+}
+
 template <int NTH = 128>
 __device__ __forceinline__ void invert_unit_lower64(float* am, int ptid) {
   if (ptid < 64) {

@@ -778,9 +778,10 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
   constexpr int BV = 32;
   const int NT = (a->T + kC - 1) / kC;
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
-  float* state = a->ht != nullptr ? a->ht : reinterpret_cast<float*>(ws);
-  uint8_t* packets = ws + state_bytes;
-  const int ns_max = int((a->workspace_bytes - state_bytes) / per_chunk);
+  unsigned int* work = reinterpret_cast<unsigned int*>(ws);
+  float* state = a->ht != nullptr ? a->ht : reinterpret_cast<float*>(ws + kWorkspaceHeaderBytes);
+  uint8_t* packets = ws + kWorkspaceHeaderBytes + state_bytes;
+  const int ns_max = int((a->workspace_bytes - kWorkspaceHeaderBytes - state_bytes) / per_chunk);
   WyParams wp;
   ScanParams sp;
   memset(&wp, 0, sizeof(wp));
@@ -793,6 +794,7 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
   wp.g = a->g;
   wp.status = sp.status = a->status;
   wp.packets = packets;
+  wp.work = work;
   sp.packets = packets;
   wp.sb_b = a->beta_stride[0];
   wp.sb_t = a->beta_stride[1];
@@ -833,6 +835,8 @@ int run_two_kernel(const gdn_fwd_args* a, void* stream, uint64_t per_chunk, uint
     const int nblk = ns / 64 < 1 ? 1 : (ns / 64 > 4 ? 4 : ns / 64);
     wp.blk_len = (ns + nblk - 1) / nblk;
     sp.h0 = (c0 == 0) ? a->h0 : state;
+    // the prep claims its items from this counter
+    if (cudaMemsetAsync(work, 0, sizeof(unsigned int), s) != cudaSuccess) return GDN_ERR_CUDA;
     int rc = run_wy(in_bf16, wp, nsm, s);
     if (rc != GDN_OK) return rc;
     rc = run_scan(a->out_dtype, sp, a->B * a->H * sp.nslice, s);
@@ -851,7 +855,8 @@ int run(const gdn_fwd_args* a, float* w_out, float* u_out, void* stream, bool pr
   if (!prep && a->workspace != nullptr) {
     const uint64_t per_chunk = uint64_t(a->B) * a->H * kPacketBytesPerChunk;
     const uint64_t state_bytes = uint64_t(a->B) * a->H * kV * kK * 4;
-    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0 && a->workspace_bytes >= state_bytes + per_chunk)
+    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0 &&
+        a->workspace_bytes >= kWorkspaceHeaderBytes + state_bytes + per_chunk)
       return run_two_kernel(a, stream, per_chunk, state_bytes);
   }
   // the single fused kernel (and the WY/UT-only mode) reads q and k as given and
@@ -946,7 +951,7 @@ extern "C" const char* gdn_status_string(int code) {
     case GDN_ERR_CUDA: return "CUDA runtime error";
     case GDN_ERR_TIMEOUT: return "device-side wait timed out (kernel aborted)";
     case GDN_ERR_NO_DEVICE: return "current device is not sm_100 (B200)";
-    case GDN_ERR_SCRATCH_LIMIT: return "request too large for the fixed no-alloc scratch (B*H*(98560+V*K*4) bytes)";
+    case GDN_ERR_SCRATCH_LIMIT: return "request too large for the fixed no-alloc scratch (256+B*H*(98560+V*K*4) bytes)";
   }
   return "unknown status";
 }
@@ -956,7 +961,8 @@ extern "C" int gdn_abi_version(void) { return GDN_B200_ABI_VERSION; }
 extern "C" uint64_t gdn_fwd_workspace_bytes(const gdn_fwd_args* a) {
   if (a == nullptr || a->B < 1 || a->H < 1 || a->T < 1 || a->chunk_size != gdn::kC) return 0;
   const uint64_t nt = (uint64_t(a->T) + gdn::kC - 1) / gdn::kC;
-  return uint64_t(a->B) * a->H * (nt * gdn::kPacketBytesPerChunk + uint64_t(gdn::kV) * gdn::kK * 4);
+  return gdn::kWorkspaceHeaderBytes +
+         uint64_t(a->B) * a->H * (nt * gdn::kPacketBytesPerChunk + uint64_t(gdn::kV) * gdn::kK * 4);
 }
 
 #ifdef GDN_TRACE

@@ -23,8 +23,9 @@
 // entry point must not be used after one.
 //
 // Every call uses the same array and leaves the last call's data in it.  The
-// kernels never read a scratch byte that the same call has not written first,
-// so nothing has to start at zero.  Calls that can run at the same time on the
+// kernels never read a scratch byte that the same call has not written first
+// (the work counter in the array's first bytes is zeroed by the call itself,
+// before each prep launch), so nothing has to start at zero.  Calls that can run at the same time on the
 // GPU (different streams, or different host threads on one device) race on
 // the array: serialise them.
 #include "../../include/gdn_b200.h"
@@ -75,7 +76,7 @@ extern "C" int gdn_fwd_sm100_noalloc(const gdn_fwd_args* args, void* stream) {
   // the sequence is then processed in as many segments as the array needs.
   const uint64_t pairs = uint64_t(args->B) * uint64_t(args->H);
   const uint64_t per_pair = gdn::kPacketBytesPerChunk + uint64_t(args->K) * uint64_t(args->V) * 4ull;
-  if (pairs > gdn::kScratchBytes / per_pair) return GDN_ERR_SCRATCH_LIMIT;
+  if (pairs > (gdn::kScratchBytes - gdn::kWorkspaceHeaderBytes) / per_pair) return GDN_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   const int rc = gdn::scratch_for_current_device(&scratch);
   if (rc != GDN_OK) return rc;

@@ -89,9 +89,10 @@ static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
 // many packets as fit are still in L2 when the scan reads them (the scan loads
 // its private c / o_intra slices evict-first); measured 1.3 % per forward.
 //
-// The kernel is persistent: CTA x takes the items (chunks) x, x + G, x + 2G, ...
-// of the grid's G CTAs, so the items in flight at any time are a contiguous
-// range, as with one CTA per item.  Each mbarrier completes one phase per item
+// The kernel is persistent: its CTAs claim items (chunks) in order from a
+// counter in the workspace, one item ahead of the one they run, so the items in
+// flight at any time are a contiguous range, as with one CTA per item, and
+// no SM is left with a single CTA at the end.  Each mbarrier completes one phase per item
 // (B_NSR / B_NSD an even number), so an item's phases have parity (item & 1).
 // The next item's inputs are loaded while this one finishes, each as soon as
 // its buffer is free: k after epilogue A (Kbar is out), q after epilogue C,
@@ -297,9 +298,10 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + wy::misc + 4);
   float* amat = reinterpret_cast<float*>(sm + wy::amat);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int G = int(gridDim.x);
   const int nitems = P.B * P.H * P.NS;
-  const int my_n = int(blockIdx.x) < nitems ? (nitems - 1 - int(blockIdx.x)) / G + 1 : 0;
+  // item of each parity slot, written by the MMA warp before its B_VEC arrival
+  // (-1: no further item, the prep warps leave)
+  volatile int* slot_item = reinterpret_cast<volatile int*>(sm + wy::misc + 8);
 
   if (warp == wy::kMmaWarp) {
     if (lane == 0) {
@@ -348,25 +350,37 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       }
       ++nv;
     };
+    // items are claimed one ahead from the segment's counter (zeroed before
+    // the launch), so CTAs that run faster take more items and all finish
+    // together (a fixed round-robin left one CTA per SM running the last
+    // items alone)
+    auto claim = [&]() -> int {
+      int x = 0;
+      if (lane == 0) x = int(atomicAdd(P.work, 1u));
+      return __shfl_sync(0xffffffffu, x, 0);
+    };
     bool ok = true;
-    if (my_n > 0) {
+    int cur = claim();
+    if (cur < nitems) {
       int il, bh;
-      wy_item<kBlocked>(P, blockIdx.x, il, bh);
+      wy_item<kBlocked>(P, cur, il, bh);
       const int t0 = (P.c0 + il) * kC, hh = bh % P.H, bb = bh / P.H;
       load_k(t0, hh, bb);
       load_q(t0, hh, bb);
       load_v(t0, hh, bb);
       wy_vectors(wy_step_vals(P, bb, hh, t0, lane), vec_buf, lane);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[wy::B_VEC]);
     }
-    for (int it = 0; it < my_n && ok; ++it) {
+    if (lane == 0) slot_item[0] = cur < nitems ? cur : -1;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars[wy::B_VEC]);
+    for (int it = 0; cur < nitems && ok; ++it) {
       const uint32_t ph = uint32_t(it) & 1u;
-      const bool has_next = it + 1 < my_n;
+      const int next = claim();
+      const bool has_next = next < nitems;
       int nt0 = 0, nhh = 0, nbb = 0;
       if (has_next) {
         int nil, nbh;
-        wy_item<kBlocked>(P, int(blockIdx.x) + (it + 1) * G, nil, nbh);
+        wy_item<kBlocked>(P, next, nil, nbh);
         nt0 = (P.c0 + nil) * kC;
         nhh = nbh % P.H;
         nbb = nbh / P.H;
@@ -392,15 +406,17 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         mma_f16_ss_warp(tmem, sdesc(a, 16, 1024, kSw128), sdesc(a, 16, 1024, kSw128), id_s, kk > 0);
       }
       mma_commit_warp(&bars[wy::B_SFULL]);
-      if (has_next) {
-        // the next item's vectors into the other buffer, while the prep warps
-        // run A / P and the inverse: that buffer's previous item read it for
-        // the last time in its epilogue C, and B_STARTED says every prep warp
-        // has waited on this item's B_VEC phase
-        const WyStepVals nsv = wy_step_vals(P, nbb, nhh, nt0, lane);
+      {
+        // the next item (or the end) for the prep warps, with its vectors in
+        // the other buffer, while they run A / P and the inverse: that buffer's
+        // previous item read it for the last time in its epilogue C, and
+        // B_STARTED says every prep warp has waited on this item's B_VEC phase
+        WyStepVals nsv = {0.f, 0.f, 0.f, 0.f};
+        if (has_next) nsv = wy_step_vals(P, nbb, nhh, nt0, lane);
         ok = mbar_wait_warp(&bars[wy::B_STARTED], ph, abort_flag);
         if (!ok) break;
-        wy_vectors(nsv, vec_buf + (ph ^ 1u) * (wy::kVecBytes / 4), lane);
+        if (has_next) wy_vectors(nsv, vec_buf + (ph ^ 1u) * (wy::kVecBytes / 4), lane);
+        if (lane == 0) slot_item[ph ^ 1u] = has_next ? next : -1;
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[wy::B_VEC]);
       }
@@ -479,6 +495,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
         if (!ok) break;
         load_v(nt0, nhh, nbb);
       }
+      cur = next;
     }
     if (!ok && lane == 0) *abort_flag = 1;
     __syncwarp();
@@ -498,14 +515,16 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
     const int ptid = tid;                     // 0..255
     const int lq = warp & 3, hc = warp >> 2;  // TMEM lane quarter, column half
     const int r = (lq << 5) | lane;           // TMEM lane = row of an M=128 accumulator
-    for (int it = 0; it < my_n; ++it) {
+    for (int it = 0;; ++it) {
       const uint32_t ph = uint32_t(it) & 1u;
-      int il, bh;
-      wy_item<kBlocked>(P, int(blockIdx.x) + it * G, il, bh);
-      uint8_t* const pkg = P.packets + (size_t(bh) * P.NS + il) * kPacketBytes;
-      const float* vec = reinterpret_cast<const float*>(sm + wy::vec + ph * wy::kVecBytes);
       bool ok = mbar_wait_warp(&bars[wy::B_VEC], ph, abort_flag);
       if (bar_any(1, NP, !ok || *abort_flag)) break;
+      const int x = slot_item[ph];
+      if (x < 0) break;  // the same value for every prep warp: no further item
+      int il, bh;
+      wy_item<kBlocked>(P, x, il, bh);
+      uint8_t* const pkg = P.packets + (size_t(bh) * P.NS + il) * kPacketBytes;
+      const float* vec = reinterpret_cast<const float*>(sm + wy::vec + ph * wy::kVecBytes);
       if (lane == 0) mbar_arrive(&bars[wy::B_STARTED]);
       const float b2first = vec[V_B2 * kC], b2last = vec[V_B2 * kC + kC - 1];
       const float ref = 0.5f * (b2first + b2last);
@@ -588,7 +607,9 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
           ok = ns_solve64<NP>(amat, sm + wy::tw, sm + wy::tw + 8192, sm + wy::zz, tmem, &bars[wy::B_NSR],
                               &bars[wy::B_NSD], (P.flags >> GDN_FLAG_NS_ITERS_SHIFT) & 15, abort_flag);
         else
-          invert_unit_lower64<NP>(amat, ptid);  // T = (I + A)^-1 in place
+          // T = (I + A)^-1 in place; the doubling intermediates go to the
+          // T operand buffer, unused until the split below
+          invert_unit_lower64_scr<NP>(amat, reinterpret_cast<float*>(sm + wy::tw), ptid);
         if (!ok) break;  // uniform: ns_solve64 decides through bar_any
         // Tw = T diag(beta e^b), Tb = T diag(beta), each split hi + lo in the input dtype:
         // [Tw_hi; Tb_hi] and [Tw_lo; Tb_lo]
@@ -661,21 +682,26 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
             }
           }
         }
-        {
+        if (isw) {
+          // Kbar, both 64-column blocks of row t, by the W-row warps only: the
+          // U-row warps carry the hi / lo split above, the larger share
           const float dd = vec[V_DD * kC + t];
-          const uint8_t* ks = sm + (isw ? wy::k0 : wy::k1);
-          uint8_t* kd = sm + wy::kbar + (isw ? 0 : 8192);
 #pragma unroll
-          for (int c = 4 * hc; c < 4 * hc + 4; ++c) {
-            const uint4 x = *reinterpret_cast<const uint4*>(ks + sw128_off(t, c));
-            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-            uint32_t ys[4];
+          for (int b = 0; b < 2; ++b) {
+            const uint8_t* ks = sm + (b ? wy::k1 : wy::k0);
+            uint8_t* kd = sm + wy::kbar + b * 8192;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = Cvt<InT>::unpack(xs[e]);
-              ys[e] = Cvt<__half>::pack(f.x * dd, f.y * dd);
+            for (int c = 4 * hc; c < 4 * hc + 4; ++c) {
+              const uint4 x = *reinterpret_cast<const uint4*>(ks + sw128_off(t, c));
+              const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+              uint32_t ys[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = Cvt<InT>::unpack(xs[e]);
+                ys[e] = Cvt<__half>::pack(f.x * dd, f.y * dd);
+              }
+              *reinterpret_cast<uint4*>(kd + sw128_off(t, c)) = make_uint4(ys[0], ys[1], ys[2], ys[3]);
             }
-            *reinterpret_cast<uint4*>(kd + sw128_off(t, c)) = make_uint4(ys[0], ys[1], ys[2], ys[3]);
           }
         }
         fence_async_smem();

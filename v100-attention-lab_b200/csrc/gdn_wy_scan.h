@@ -16,6 +16,7 @@ struct WyParams {
   const float* beta;
   const float* g;
   uint8_t* packets;  // NS packets per (b, h)
+  unsigned int* work;  // item counter, zero at launch
   int* status;
   long long* trace;  // GDN_TRACE builds: phase timestamps of CTAs 0-63
   long long sb_b, sb_t, sb_h;
@@ -40,6 +41,8 @@ struct ScanParams {
 
 // Bytes of one packet: N and Q' images, e^{b_C}, c and o_intra slices (fp16).
 constexpr uint64_t kPacketBytesPerChunk = 98560;
+// Workspace header (the prep's item counter) before the state area and packets.
+constexpr uint64_t kWorkspaceHeaderBytes = 256;
 
 // Launch the prep over the segment's B * H * NS items with min(items, 2 * SMs) CTAs.
 int run_wy(int in_bf16, const WyParams& p, int num_sms, cudaStream_t s);

@@ -37,6 +37,7 @@ NS_ITERS_SHIFT = 8       # its iteration count, 1..15, in bits 8-11
 # Scratch bytes of the two-kernel path per (batch, head, chunk of 64 steps);
 # gdn_fwd_workspace_bytes() is the authority, this mirrors it for sizing.
 PACKET_BYTES_PER_CHUNK = 98560
+WORKSPACE_HEADER_BYTES = 256  # the prep's item counter, ahead of the state area and packets
 
 # Every symbol include/gdn_b200.h declares.
 EXPORTED_SYMBOLS = ("gdn_fwd_sm100", "gdn_fwd_sm100_noalloc", "gdn_fwd_workspace_bytes", "gdn_wy_prep_sm100",

@@ -39,7 +39,7 @@ _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 # Upper bound of the scratch of the two-kernel path per (device, stream);
 # longer inputs run in several segments of chunks, so memory does not grow
 # with T.
-WORKSPACE_CAP_BYTES = int(os.environ.get("GDN_B200_WORKSPACE_MB", "1024")) << 20
+WORKSPACE_CAP_BYTES = int(os.environ.get("GDN_B200_WORKSPACE_MB", "4096")) << 20
 
 
 def _workspace(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor:
@@ -248,7 +248,7 @@ def gdn_chunk_fwd(q, k, v, beta, g, initial_state=None, chunk_size=64, *, output
         stream = torch.cuda.current_stream(dev)
         if not fused:
             need = int(lib.gdn_fwd_workspace_bytes(ctypes.byref(args)))
-            per_head = B * H * (_lib.PACKET_BYTES_PER_CHUNK + V * K * 4)
+            per_head = _lib.WORKSPACE_HEADER_BYTES + B * H * (_lib.PACKET_BYTES_PER_CHUNK + V * K * 4)
             nbytes = max(min(need, WORKSPACE_CAP_BYTES), per_head)
             ws = _workspace(dev, stream, nbytes)
             args.workspace = ws.data_ptr()
