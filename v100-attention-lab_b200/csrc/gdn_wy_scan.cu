@@ -350,31 +350,51 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       }
       ++nv;
     };
-    // items are claimed one ahead from the segment's counter (zeroed before
-    // the launch), so CTAs that run faster take more items and all finish
-    // together (a fixed round-robin left one CTA per SM running the last
-    // items alone)
+    // Each CTA's first item is its blockIdx (no atomic on the path of the
+    // first item, which all CTAs start at once); the items after the first
+    // G are claimed one ahead from the segment's counter (zeroed before the
+    // launch), so CTAs that run faster take more items and all finish together
+    // (a fixed round-robin left one CTA per SM running the last items alone).
     auto claim = [&]() -> int {
       int x = 0;
-      if (lane == 0) x = int(atomicAdd(P.work, 1u));
+      if (lane == 0) x = int(atomicAdd(P.work, 1u)) + int(gridDim.x);
       return __shfl_sync(0xffffffffu, x, 0);
     };
     bool ok = true;
-    int cur = claim();
+    int cur = int(blockIdx.x);
     if (cur < nitems) {
       int il, bh;
       wy_item<kBlocked>(P, cur, il, bh);
       const int t0 = (P.c0 + il) * kC, hh = bh % P.H, bb = bh / P.H;
+      // g and beta first: these small loads would otherwise queue behind
+      // the whole grid's q / k / v tiles (measured: the first vectors took
+      // ~9k cycles after the CTA started)
+      const WyStepVals sv0 = wy_step_vals(P, bb, hh, t0, lane);
       load_k(t0, hh, bb);
       load_q(t0, hh, bb);
       load_v(t0, hh, bb);
-      wy_vectors(wy_step_vals(P, bb, hh, t0, lane), vec_buf, lane);
+      wy_vectors(sv0, vec_buf, lane);
     }
     if (lane == 0) slot_item[0] = cur < nitems ? cur : -1;
     __syncwarp();
     if (lane == 0) mbar_arrive(&bars[wy::B_VEC]);
     for (int it = 0; cur < nitems && ok; ++it) {
       const uint32_t ph = uint32_t(it) & 1u;
+      ok = mbar_wait_warp(&bars[wy::B_FULLK], ph, abort_flag) && mbar_wait_warp(&bars[wy::B_FULLQ], ph, abort_flag);
+      if (P.flags & GDN_FLAG_QK_L2NORM) ok = ok && mbar_wait_warp(&bars[wy::B_NORM], ph, abort_flag);
+      if (it > 0) ok = ok && mbar_wait_warp(&bars[wy::B_EPB], ph ^ 1u, abort_flag);  // TMEM released
+      if (!ok) break;
+      // S = [K;Q] K^T: M=128 (k rows then q rows), N=64, K=128
+      tc_fence_after();
+      const uint32_t id_s = idesc_f16(128, 64, kInBf16, 0, 0);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t a = sb + wy::k0 + (kk >> 2) * 16384 + (kk & 3) * 32;
+        mma_f16_ss_warp(tmem, sdesc(a, 16, 1024, kSw128), sdesc(a, 16, 1024, kSw128), id_s, kk > 0);
+      }
+      mma_commit_warp(&bars[wy::B_SFULL]);
+      // the next item, claimed after this S product is issued so that the
+      // claim's atomic never delays it
       const int next = claim();
       const bool has_next = next < nitems;
       int nt0 = 0, nhh = 0, nbb = 0;
@@ -393,19 +413,6 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
           tma_prefetch_4d(&P.tm_v, 64, nt0, nhh, nbb);
         }
       }
-      ok = mbar_wait_warp(&bars[wy::B_FULLK], ph, abort_flag) && mbar_wait_warp(&bars[wy::B_FULLQ], ph, abort_flag);
-      if (P.flags & GDN_FLAG_QK_L2NORM) ok = ok && mbar_wait_warp(&bars[wy::B_NORM], ph, abort_flag);
-      if (it > 0) ok = ok && mbar_wait_warp(&bars[wy::B_EPB], ph ^ 1u, abort_flag);  // TMEM released
-      if (!ok) break;
-      // S = [K;Q] K^T: M=128 (k rows then q rows), N=64, K=128
-      tc_fence_after();
-      const uint32_t id_s = idesc_f16(128, 64, kInBf16, 0, 0);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t a = sb + wy::k0 + (kk >> 2) * 16384 + (kk & 3) * 32;
-        mma_f16_ss_warp(tmem, sdesc(a, 16, 1024, kSw128), sdesc(a, 16, 1024, kSw128), id_s, kk > 0);
-      }
-      mma_commit_warp(&bars[wy::B_SFULL]);
       {
         // the next item (or the end) for the prep warps, with its vectors in
         // the other buffer, while they run A / P and the inverse: that buffer's
