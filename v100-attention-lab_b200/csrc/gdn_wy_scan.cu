@@ -837,17 +837,22 @@ constexpr uint32_t alloc = total + 1024;
 static_assert(alloc <= 232448, "shared memory budget exceeded");
 static_assert(kOffO + 4096 <= kSlotB && kOffHdr + 256 <= kOffC && kSlotB % 1024 == 0, "slot layout");
 static_assert(pkt::kQ + 16384 == pkt::kHdr, "Q' and hdr adjacent in the packet");
-constexpr uint32_t kTmN = 0, kTmO = 32;  // N S (M=128, 32 cols); Q' S (M=64) x 2 buffers
+// TMEM: N S (M=128, 32 cols) and Q' S (M=64) in 3 rotating buffers.  The output
+// product of chunk c is issued once S'(c+1) is ready (the last one once S'(c)
+// is); the chain warps read chunk c-3 out of the same buffer before that.
+constexpr uint32_t kTmN = 0, kTmO = 32;
+constexpr int kOBufs = 3;
+static_assert(kTmO + kOBufs * 32 <= 128, "TMEM columns");
 enum {
   B_FULLA = 0,    // [3] N landed
   B_FULLB = 3,    // [3] Q', hdr, c, o_intra landed
   B_EMPTYA = 6,   // [3] N S of the slot's chunk complete (MMA commit)
   B_EMPTYB = 9,   // [3] output MMA commit + 4 chain warps
   B_DN = 12,      // N S of the current chunk complete
-  B_DO = 13,      // [2] Q' S of a chunk complete
-  B_SREADY = 15,  // S16 of the next chunk written (4 chain warps)
-  B_DONE = 16,
-  B_COUNT = 17
+  B_DO = 13,      // [3] Q' S of a chunk complete
+  B_SREADY = 16,  // S16 of the next chunk written (4 chain warps)
+  B_DONE = 17,
+  B_COUNT = 18
 };
 }  // namespace sc
 
@@ -942,9 +947,9 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
       const uint32_t sbuf = sb + sc::s16 + (c % sc::kSBufs) * 8192;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ss_warp(tmem + sc::kTmO + (c & 1) * BV, sdesc(st + sc::kOffQ + kk * 2048, 1024, 128, kSwNone),
+        mma_f16_ss_warp(tmem + sc::kTmO + (c % sc::kOBufs) * BV, sdesc(st + sc::kOffQ + kk * 2048, 1024, 128, kSwNone),
                         sdesc(sbuf + kk * 1024, 8192, 512, kSw64), id_o, kk > 0);
-      mma_commit_warp(&bars[sc::B_DO + (c & 1)]);
+      mma_commit_warp(&bars[sc::B_DO + c % sc::kOBufs]);
       mma_commit_warp(&bars[sc::B_EMPTYB + s]);
       return true;
     };
@@ -998,10 +1003,10 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
     // output rows of chunk c: o = Q' S + o_intra (gdn_ref.py:86-90); rows t = 16 w + l (l < 16)
     auto out_rows = [&](int c) -> bool {
       const int s = c % sc::kStages;
-      if (!mbar_wait_warp(&bars[sc::B_DO + (c & 1)], (c >> 1) & 1, abort_flag)) return false;
+      if (!mbar_wait_warp(&bars[sc::B_DO + c % sc::kOBufs], (c / sc::kOBufs) & 1, abort_flag)) return false;
       tc_fence_after();
       float ov[BV];
-      tmem_ld32w(tmem_addr(tmem + sc::kTmO + (c & 1) * BV, warp * 32, 0), ov);
+      tmem_ld32w(tmem_addr(tmem + sc::kTmO + (c % sc::kOBufs) * BV, warp * 32, 0), ov);
       tc_fence_before();
       const int t = 16 * warp + lane;
       const int tg = (P.c0 + c) * kC + t;
