@@ -96,8 +96,9 @@ static_assert(2 * (alloc + 1024) <= 233472, "two CTAs per SM");
 // (B_NSR / B_NSD an even number), so an item's phases have parity (item & 1).
 // The next item's inputs are loaded while this one finishes, each as soon as
 // its buffer is free: k after epilogue A (Kbar is out), q after epilogue C,
-// v (later U_lo) after the N / c products; its S product waits for epilogue B
-// to release TMEM.  Its g and beta are read and its vectors written (into the
+// v (later U_lo) after the N / c products; its S product (TMEM columns 0-63)
+// is issued as soon as epilogue B has read those columns, while the rest of
+// epilogue B runs.  Its g and beta are read and its vectors written (into the
 // other of two buffers) right after this item's S product is issued, while the
 // prep warps run the inverse, so neither the next S product nor the MMA
 // warp's response to the epilogues waits on them (measured: vectors computed
@@ -117,7 +118,7 @@ enum {
   B_PFULL,
   B_EPC,
   B_NCFULL,
-  B_EPB,        // epilogue B has read N and c: TMEM free for the next item
+  B_EPB,        // epilogue B has read TMEM columns 0-63 (warps 0-3): the next S may go there
   B_NORM,
   B_NSR,
   B_NSD,
@@ -306,10 +307,10 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
   if (warp == wy::kMmaWarp) {
     if (lane == 0) {
       for (int i = 0; i < wy::B_COUNT; ++i)
-        mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC || i == wy::B_EPB ||
-                             i == wy::B_NORM || i == wy::B_NSR || i == wy::B_STARTED)
+        mbar_init(&bars[i], (i == wy::B_TREADY || i == wy::B_EPA || i == wy::B_EPC || i == wy::B_NORM ||
+                             i == wy::B_NSR || i == wy::B_STARTED)
                                 ? wy::kPrep / 32
-                                : 1);
+                                : (i == wy::B_EPB ? wy::kPrep / 64 : 1));
       *abort_flag = 0;
       fence_mbar_init();
     }
@@ -382,7 +383,7 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       const uint32_t ph = uint32_t(it) & 1u;
       ok = mbar_wait_warp(&bars[wy::B_FULLK], ph, abort_flag) && mbar_wait_warp(&bars[wy::B_FULLQ], ph, abort_flag);
       if (P.flags & GDN_FLAG_QK_L2NORM) ok = ok && mbar_wait_warp(&bars[wy::B_NORM], ph, abort_flag);
-      if (it > 0) ok = ok && mbar_wait_warp(&bars[wy::B_EPB], ph ^ 1u, abort_flag);  // TMEM released
+      if (it > 0) ok = ok && mbar_wait_warp(&bars[wy::B_EPB], ph ^ 1u, abort_flag);  // columns 0-63 read
       if (!ok) break;
       // S = [K;Q] K^T: M=128 (k rows then q rows), N=64, K=128
       tc_fence_after();
@@ -785,6 +786,11 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
             st_global_hint(pkg + pkt::kN + (j * 128 + r) * 16, pack8_f16(n + 8 * c), keep);
           }
         }
+        if (hc == 0) {  // columns 0-63 read: the next item's S product may overwrite them
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[wy::B_EPB]);
+        }
 #pragma unroll 1
         for (int c0 = 64 * hc; c0 < 64 * hc + 64; c0 += 32) {
           float cv[32];
@@ -794,8 +800,6 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
           for (int c = 0; c < 4; ++c) st_global_hint(dst + (c * 128 + r) * 16, pack8_f16(cv + 8 * c), keep);
         }
         tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[wy::B_EPB]);
       }
     }
   }
