@@ -290,6 +290,43 @@ __device__ __forceinline__ void wy_vectors(const WyStepVals& sv, float* vec, int
   vec[V_DD * kC + lane + 32] = fast_exp2(bC - xb);
 }
 
+// q/k L2 normalisation in the kernel (gdn_ref.py:24-25): every row of the raw
+// q and k tiles divided by sqrt(sum of squares + 1e-6) in fp32, in place.
+// Thread pair (2i, 2i+1) takes the two 64-column blocks of row i (k rows, then
+// q rows).  Out of line: inlined, its registers pushed the rest of the kernel
+// into spills (the kernel runs at 96 registers for two CTAs per SM).
+template <typename InT>
+__device__ __noinline__ void l2norm_qk_rows(uint8_t* sm, int ptid) {
+  const int rr = ptid >> 1, half = ptid & 1, t = rr & 63;
+  uint8_t* blk = sm + (rr < 64 ? wy::k0 : wy::q0) + half * 16384;
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint4 x = *reinterpret_cast<const uint4*>(blk + sw128_off(t, c));
+    const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = Cvt<InT>::unpack(w4[e]);
+      ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+    }
+  }
+  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+  const float inv = 1.f / sqrtf(ss + 1e-6f);
+  // second pass re-reads the row from shared memory rather than holding it
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint4 x = *reinterpret_cast<const uint4*>(blk + sw128_off(t, c));
+    const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+    uint32_t y4[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = Cvt<InT>::unpack(w4[e]);
+      y4[e] = Cvt<InT>::pack(f.x * inv, f.y * inv);
+    }
+    *reinterpret_cast<uint4*>(blk + sw128_off(t, c)) = make_uint4(y4[0], y4[1], y4[2], y4[3]);
+  }
+}
+
 template <typename InT, bool kBlocked>
 __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_constant__ WyParams P) {
   extern __shared__ uint8_t smem_raw[];
@@ -540,37 +577,9 @@ __global__ void __launch_bounds__(wy::kThreads, 2) gdn_wy_kernel(const __grid_co
       if (ptid < 64) amat[ptid * kAStride + 64] = fast_exp2(ref - vec[V_B2 * kC + ptid]);
       named_bar(2, NP);
       if (P.flags & GDN_FLAG_QK_L2NORM) {
-        // raw q and k: every row divided by sqrt(sum of squares + 1e-6) in fp32, in
-        // place, before any product reads them (gdn_ref.py:24-25).  Thread pair
-        // (2i, 2i+1) takes the two 64-column blocks of row i (k rows, then q rows).
+        // raw q and k normalised in place before any product reads them
         if (mbar_wait_warp(&bars[wy::B_FULLK], ph, abort_flag) && mbar_wait_warp(&bars[wy::B_FULLQ], ph, abort_flag)) {
-          const int rr = ptid >> 1, half = ptid & 1, t = rr & 63;
-          uint8_t* blk = sm + (rr < 64 ? wy::k0 : wy::q0) + half * 16384;
-          uint4 xv[8];
-          float ss = 0.f;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            xv[c] = *reinterpret_cast<const uint4*>(blk + sw128_off(t, c));
-            const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = Cvt<InT>::unpack(w4[e]);
-              ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
-            }
-          }
-          ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-          const float inv = 1.f / sqrtf(ss + 1e-6f);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint32_t w4[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
-            uint32_t y4[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = Cvt<InT>::unpack(w4[e]);
-              y4[e] = Cvt<InT>::pack(f.x * inv, f.y * inv);
-            }
-            *reinterpret_cast<uint4*>(blk + sw128_off(t, c)) = make_uint4(y4[0], y4[1], y4[2], y4[3]);
-          }
+          l2norm_qk_rows<InT>(sm, ptid);
         }
         fence_async_smem();
         __syncwarp();
