@@ -833,16 +833,18 @@ namespace sc {
 // warps 0-3: state chain + output rows (TMEM lane quarters), warp 4: ring A loads,
 // warp 5: every tcgen05.mma of the CTA, warp 6: ring B loads
 constexpr int kThreads = 224;
-constexpr int kStages = 3;
+// ring B is freed only once the output rows of its chunk are out, two chunks
+// after the chunk's state update, hence the deeper ring
+constexpr int kStagesA = 2, kStagesB = 4;
 // ring A slot: N (32 KB), free once N S of its chunk completed
 // ring B slot: [Q' 16 KB | hdr] (one bulk copy), this CTA's c and o_intra slices
 constexpr uint32_t kSlotA = 32768;
 constexpr uint32_t kOffQ = 0, kOffHdr = 16384, kOffC = 17408, kOffO = 25600;
 constexpr uint32_t kSlotB = 29696;
 constexpr uint32_t ringA = 0;
-constexpr uint32_t ringB = kStages * kSlotA;
+constexpr uint32_t ringB = kStagesA * kSlotA;
 constexpr int kSBufs = 3;                   // S fp16 [k][v] MN-major SW64, 8 KB each
-constexpr uint32_t s16 = ringB + kStages * kSlotB;
+constexpr uint32_t s16 = ringB + kStagesB * kSlotB;
 constexpr uint32_t bars = s16 + kSBufs * 8192;
 constexpr uint32_t misc = bars + 24 * 8;
 constexpr uint32_t total = misc + 32;
@@ -857,11 +859,11 @@ constexpr uint32_t kTmN = 0, kTmO = 32;
 constexpr int kOBufs = 3;
 static_assert(kTmO + kOBufs * 32 <= 128, "TMEM columns");
 enum {
-  B_FULLA = 0,    // [3] N landed
-  B_FULLB = 3,    // [3] Q', hdr, c, o_intra landed
-  B_EMPTYA = 6,   // [3] N S of the slot's chunk complete (MMA commit)
-  B_EMPTYB = 9,   // [3] output MMA commit + 4 chain warps
-  B_DN = 12,      // N S of the current chunk complete
+  B_FULLA = 0,    // [2] N landed
+  B_FULLB = 2,    // [4] Q', hdr, c, o_intra landed
+  B_EMPTYA = 6,   // [2] N S of the slot's chunk complete (MMA commit)
+  B_EMPTYB = 8,   // [4] output MMA commit + 4 chain warps
+  B_DN = 12,      // N S of the current chunk complete (and every earlier product)
   B_DO = 13,      // [3] Q' S of a chunk complete
   B_SREADY = 16,  // S16 of the next chunk written (4 chain warps)
   B_DONE = 17,
@@ -890,7 +892,7 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
 
   if (tid == 0) {
     for (int i = 0; i < sc::B_COUNT; ++i) {
-      const bool emptyb = i >= sc::B_EMPTYB && i < sc::B_EMPTYB + 3;
+      const bool emptyb = i >= sc::B_EMPTYB && i < sc::B_EMPTYB + sc::kStagesB;
       mbar_init(&bars[i], emptyb ? 5 : (i == sc::B_SREADY ? 4 : 1));
     }
     *abort_flag = 0;
@@ -909,10 +911,11 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
     const bool ra = warp == 4;
     const int fullb = ra ? sc::B_FULLA : sc::B_FULLB;
     const int emptyb = ra ? sc::B_EMPTYA : sc::B_EMPTYB;
+    const int nst = ra ? sc::kStagesA : sc::kStagesB;
     int issued = 0;
     for (int i = 0; i < NT; ++i) {
-      const int s = i % sc::kStages;
-      if (i >= sc::kStages && !mbar_wait_warp(&bars[emptyb + s], ((i / sc::kStages) - 1) & 1, abort_flag)) break;
+      const int s = i % nst;
+      if (i >= nst && !mbar_wait_warp(&bars[emptyb + s], ((i / nst) - 1) & 1, abort_flag)) break;
       if (lane == 0) {
         uint64_t* fb = &bars[fullb + s];
         const uint8_t* pk = P.packets + (size_t(bh) * P.NS + i) * kPacketBytes;
@@ -944,8 +947,8 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
     if (lane == 0) {
       // let every issued copy land before the CTA exits
       volatile int never = 0;
-      for (int i = (issued > sc::kStages ? issued - sc::kStages : 0); i < issued; ++i)
-        mbar_wait(&bars[fullb + i % sc::kStages], (i / sc::kStages) & 1, &never);
+      for (int i = (issued > nst ? issued - nst : 0); i < issued; ++i)
+        mbar_wait(&bars[fullb + i % nst], (i / nst) & 1, &never);
     }
     __syncwarp();
   } else if (warp == 5) {
@@ -953,8 +956,8 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
     const uint32_t id_n = idesc_f16(128, BV, 0, 0, 1);
     const uint32_t id_o = idesc_f16(64, BV, 0, 0, 1);
     auto issue_out = [&](int c) -> bool {
-      const int s = c % sc::kStages;
-      if (!mbar_wait_warp(&bars[sc::B_FULLB + s], (c / sc::kStages) & 1, abort_flag)) return false;
+      const int s = c % sc::kStagesB;
+      if (!mbar_wait_warp(&bars[sc::B_FULLB + s], (c / sc::kStagesB) & 1, abort_flag)) return false;
       tc_fence_after();
       const uint32_t st = sb + sc::ringB + s * sc::kSlotB;
       const uint32_t sbuf = sb + sc::s16 + (c % sc::kSBufs) * 8192;
@@ -968,7 +971,7 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
     };
     bool okm = true;
     for (int c = 0; c < NT && okm; ++c) {
-      const int s = c % sc::kStages;
+      const int s = c % sc::kStagesA;
       // descriptors first: after S' is ready only the issue itself remains
       const uint32_t st = sb + sc::ringA + s * sc::kSlotA;
       const uint32_t sbuf = sb + sc::s16 + (c % sc::kSBufs) * 8192;
@@ -978,7 +981,7 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
         ad[kk] = sdesc(st + kk * 4096, 2048, 128, kSwNone);
         bd[kk] = sdesc(sbuf + kk * 1024, 8192, 512, kSw64);
       }
-      okm = mbar_wait_warp(&bars[sc::B_FULLA + s], (c / sc::kStages) & 1, abort_flag);
+      okm = mbar_wait_warp(&bars[sc::B_FULLA + s], (c / sc::kStagesA) & 1, abort_flag);
       if (lane == 0) GDN_TR(5, c);
       okm = okm && mbar_spin_warp(&bars[sc::B_SREADY], c & 1, abort_flag);
       if (!okm) break;
@@ -1013,14 +1016,10 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
 #pragma unroll
       for (int j = 0; j < BV; ++j) S[j] = 0.f;
     }
-    // output rows of chunk c: o = Q' S + o_intra (gdn_ref.py:86-90); rows t = 16 w + l (l < 16)
-    auto out_rows = [&](int c) -> bool {
-      const int s = c % sc::kStages;
-      if (!mbar_wait_warp(&bars[sc::B_DO + c % sc::kOBufs], (c / sc::kOBufs) & 1, abort_flag)) return false;
-      tc_fence_after();
-      float ov[BV];
-      tmem_ld32w(tmem_addr(tmem + sc::kTmO + (c % sc::kOBufs) * BV, warp * 32, 0), ov);
-      tc_fence_before();
+    // output rows of chunk c: o = Q' S + o_intra (gdn_ref.py:86-90); rows t = 16 w + l (l < 16).
+    // ov holds Q' S(c), read out of TMEM beforehand.
+    auto finish_out = [&](int c, float* ov) {
+      const int s = c % sc::kStagesB;
       const int t = 16 * warp + lane;
       const int tg = (P.c0 + c) * kC + t;
       const uint8_t* st = sm + sc::ringB + s * sc::kSlotB;
@@ -1041,6 +1040,14 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[sc::B_EMPTYB + s]);
+    };
+    auto out_rows = [&](int c) -> bool {
+      if (!mbar_wait_warp(&bars[sc::B_DO + c % sc::kOBufs], (c / sc::kOBufs) & 1, abort_flag)) return false;
+      tc_fence_after();
+      float ov[BV];
+      tmem_ld32w(tmem_addr(tmem + sc::kTmO + (c % sc::kOBufs) * BV, warp * 32, 0), ov);
+      tc_fence_before();
+      finish_out(c, ov);
       return true;
     };
     st_row16<BV>(sm + sc::s16, r, 0, S);
@@ -1049,9 +1056,9 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
     if (lane == 0) mbar_arrive(&bars[sc::B_SREADY]);
     bool ok = true;
     for (int i = 0; i < NT; ++i) {
-      const int s = i % sc::kStages;
+      const int s = i % sc::kStagesB;
       const uint8_t* st = sm + sc::ringB + s * sc::kSlotB;
-      ok = mbar_wait_warp(&bars[sc::B_FULLB + s], (i / sc::kStages) & 1, abort_flag);
+      ok = mbar_wait_warp(&bars[sc::B_FULLB + s], (i / sc::kStagesB) & 1, abort_flag);
       if (!ok) break;
       float cv[BV];
 #pragma unroll
@@ -1070,8 +1077,15 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
       if (!ok) break;
       tc_fence_after();
       if (r == 0) GDN_TR(2, i);
-      float d[BV];
-      tmem_ld32w(tmem_addr(tmem + sc::kTmN, warp * 32, 0), d);
+      // Q' S(i - 2) is read out of TMEM here, with N S(i): it was issued
+      // before N S(i) by the same thread, so B_DN covers it too.  The chain
+      // warps then read no TMEM while N S(i + 1) runs.
+      float d[BV], ov[BV];
+      if (i >= 2)
+        tmem_ld32x2w(tmem_addr(tmem + sc::kTmN, warp * 32, 0), d,
+                     tmem_addr(tmem + sc::kTmO + ((i - 2) % sc::kOBufs) * BV, warp * 32, 0), ov);
+      else
+        tmem_ld32w(tmem_addr(tmem + sc::kTmN, warp * 32, 0), d);
       tc_fence_before();
       // S' = e^{b_C} S + N S + c   (gdn_ref.py:92-98, regrouped)
 #pragma unroll
@@ -1083,10 +1097,10 @@ __global__ void __launch_bounds__(sc::kThreads, 1) gdn_scan_kernel(const __grid_
         if (lane == 0) mbar_arrive(&bars[sc::B_SREADY]);
       }
       if (r == 0) GDN_TR(3, i);
-      if (i > 0 && !(ok = out_rows(i - 1))) break;
+      if (i >= 2) finish_out(i - 2, ov);
       if (r == 0) GDN_TR(4, i);
     }
-    if (ok && NT > 0) ok = out_rows(NT - 1);
+    for (int c = NT >= 2 ? NT - 2 : 0; ok && c < NT; ++c) ok = out_rows(c);
     if (ok && P.ht != nullptr) {
 #pragma unroll
       for (int j = 0; j < BV; ++j) P.ht[hbase + size_t(v0 + j) * kK + r] = S[j];
